@@ -1,0 +1,352 @@
+// Frontend kernels of the listener step: PCM -> log-mel, and the streaming
+// 2x(3x3, stride 2) convolutional subsampler.
+//
+// mel_kernel restates GemmaAudioTowerBackend._extract_single_frame
+// (duplex_kernel/listener.py:1807-1850): [160-sample tail | 1280 PCM | 0] ->
+// eight 320-sample frames at hop 160, times the periodic Hann window (the
+// product is formed in fp32 exactly as the reference's float32 NumPy does),
+// 512-point real DFT magnitude, HTK mel filterbank, log(x + 1e-3).  One CTA
+// per session; the DFT uses exact twiddles from a 512-entry table.
+//
+// subsample_kernel restates the streaming subsampler
+// (duplex_kernel/streaming_conformer.py:741-761, _stream_subsample_layer
+// :1055-1068; transformers Gemma4AudioSubSampleConvProjectionLayer,
+// models/gemma4/modeling_gemma4.py:317-372): conv0 (1 -> 128 channels) +
+// LayerNorm(128) + ReLU over [cached mel row | 8 new rows], then conv1
+// (128 -> C1) + LayerNorm(C1) + ReLU over [cached conv0 row | 4 new rows].
+// conv0 runs on CUDA cores (9 taps); conv1 is an implicit GEMM
+// [64 positions x 1152] x [1152 x C1] on mma.sync bf16 tensor-core tiles with
+// fp32 accumulation.  The output is the bf16 input of the input projection.
+#include "common.cuh"
+#include "listener.h"
+
+namespace lb {
+namespace {
+
+constexpr int kFrames = 8;
+constexpr int kWin = 320;
+constexpr int kBins = 257;
+
+struct MelArgs {
+  const int* counts;
+  const int *row_slot, *row_reason;
+  const SlotMeta* row_meta;
+  const float* pcm;    // [rows][1280]
+  float* tail;         // [S][2][160]
+  float* mel;          // [rows][8][128]
+  const float *window, *cos_tab, *sin_tab, *filters;  // [320], [512], [512], [257][128]
+  const int2* filter_range;                          // [128] (k_lo, k_hi)
+};
+
+__global__ void __launch_bounds__(256) mel_kernel(MelArgs a) {
+  const int row = blockIdx.x;
+  if (row >= a.counts[0]) return;
+  __shared__ float x[kFrames * kWin];
+  __shared__ float mag[kFrames][kBins + 3];
+  __shared__ float ct[512], st[512];
+  const int slot = a.row_slot[row];
+  const int parity = (a.row_meta[row].pos >> 1) & 1;
+  // identity resets start a fresh session: no previous PCM tail
+  const bool fresh = a.row_reason[row] == 3 || a.row_reason[row] == 1;
+  const float* tail_in = a.tail + (static_cast<size_t>(slot) * 2 + parity) * kTail;
+  const float* pcm = a.pcm + static_cast<size_t>(row) * kPcm;
+  for (int i = threadIdx.x; i < 512; i += blockDim.x) {
+    ct[i] = a.cos_tab[i];
+    st[i] = a.sin_tab[i];
+  }
+  // frame f covers padded samples [160 f, 160 f + 320) of [tail | pcm | 0]
+  for (int i = threadIdx.x; i < kFrames * kWin; i += blockDim.x) {
+    const int f = i / kWin, n = i % kWin;
+    const int sidx = f * 160 + n;  // index into padded (1441 samples)
+    float v;
+    if (sidx < kTail) {
+      v = fresh ? 0.0f : tail_in[sidx];
+    } else {
+      v = pcm[sidx - kTail];  // sidx <= 7*160+319 = 1439 < 1440: never the pad sample
+    }
+    x[i] = v * a.window[n];
+  }
+  __syncthreads();
+  // staged tail for the next tick: last 160 PCM samples
+  float* tail_out = a.tail + (static_cast<size_t>(slot) * 2 + (parity ^ 1)) * kTail;
+  for (int i = threadIdx.x; i < kTail; i += blockDim.x) tail_out[i] = pcm[kPcm - kTail + i];
+  // DFT magnitudes: thread k -> bin k for all frames (bin 256 by thread 0)
+  for (int k = threadIdx.x; k < kBins; k += blockDim.x) {
+    float re[kFrames], im[kFrames];
+#pragma unroll
+    for (int f = 0; f < kFrames; ++f) re[f] = im[f] = 0.0f;
+    int idx = 0;
+    for (int n = 0; n < kWin; ++n) {
+      const float c = ct[idx], s = st[idx];
+#pragma unroll
+      for (int f = 0; f < kFrames; ++f) {
+        const float xv = x[f * kWin + n];
+        re[f] = fmaf(xv, c, re[f]);
+        im[f] = fmaf(xv, s, im[f]);
+      }
+      idx = (idx + k) & 511;
+    }
+#pragma unroll
+    for (int f = 0; f < kFrames; ++f) mag[f][k] = sqrtf(re[f] * re[f] + im[f] * im[f]);
+  }
+  __syncthreads();
+  // mel filterbank (sparse row ranges) + log
+  float* out = a.mel + static_cast<size_t>(row) * kFrames * kMelBins;
+  for (int o = threadIdx.x; o < kFrames * kMelBins; o += blockDim.x) {
+    const int f = o / kMelBins, m = o % kMelBins;
+    const int2 r = a.filter_range[m];
+    float acc = 0.0f;
+    for (int k = r.x; k < r.y; ++k) acc = fmaf(mag[f][k], a.filters[k * kMelBins + m], acc);
+    out[o] = logf(acc + 1e-3f);
+  }
+}
+
+// ------------------------------------------------------------ subsampler
+constexpr int kF0 = 64;        // conv0 output frequencies
+constexpr int kCiPad = 132;    // channel stride of the conv1 input tile (bank-conflict free)
+constexpr int kK1 = 9 * 128;   // conv1 reduction length
+constexpr int kK1Pad = kK1 + 8;
+constexpr int kSubThreads = 256;
+
+struct SubArgs {
+  const int* counts;
+  const int *row_slot, *row_mask;
+  const SlotMeta* row_meta;
+  const float* mel;             // [rows][8][128]
+  float* mel_prev;              // [S][2][128]
+  __nv_bfloat16* sub_prev;      // [S][2][64][128]
+  const float *w0, *ln0;        // [128][9], [128]
+  const __nv_bfloat16* w1;      // [C1][kK1Pad]
+  const float* ln1;             // [C1]
+  __nv_bfloat16* sub_in;        // [tok][32 * C1]  index f * C1 + c
+  float eps;
+  int c1;                       // conv1 output channels (32)
+};
+
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                               uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// C1 = 32 output channels (validated at create): 8 warps = 4 position tiles x 2 channel halves.
+__global__ void __launch_bounds__(kSubThreads, 1) subsample_kernel(SubArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sp = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) &
+                                           ~static_cast<uintptr_t>(127));
+  __nv_bfloat16* w1s = reinterpret_cast<__nv_bfloat16*>(sp);           // [32][kK1Pad]
+  __nv_bfloat16* xin = w1s + 32 * kK1Pad;                              // [5][66][kCiPad]
+  float* w0s = reinterpret_cast<float*>(xin + 5 * 66 * kCiPad);        // [128][9]
+  float* ln0s = w0s + 128 * 9;                                         // [128]
+  float* mels = ln0s + 128;                                            // [9][130]
+  float* c1out = mels + 9 * 130;                                       // [64][33]
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int i = tid; i < 32 * kK1Pad / 8; i += blockDim.x)
+    reinterpret_cast<int4*>(w1s)[i] = reinterpret_cast<const int4*>(a.w1)[i];
+  for (int i = tid; i < 128 * 9; i += blockDim.x) w0s[i] = a.w0[i];
+  for (int i = tid; i < 128; i += blockDim.x) ln0s[i] = a.ln0[i];
+  // zero the frequency padding columns of the conv1 input once (never written)
+  for (int i = tid; i < 5 * 2 * kCiPad; i += blockDim.x) {
+    const int r = i / (2 * kCiPad), side = (i / kCiPad) & 1, c = i % kCiPad;
+    xin[(r * 66 + (side ? 65 : 0)) * kCiPad + c] = __float2bfloat16_rn(0.0f);
+  }
+  const int n_rows = a.counts[0];
+  for (int row = blockIdx.x; row < n_rows; row += gridDim.x) {
+    __syncthreads();
+    const int slot = a.row_slot[row];
+    const SlotMeta m = a.row_meta[row];
+    const int parity = (m.pos >> 1) & 1;
+    const int mask = a.row_mask[row];
+    const float mel_prev_ok = (m.flags & 1) ? 1.0f : 0.0f;
+    const float sub_prev_ok = (m.flags & 2) ? 1.0f : 0.0f;
+    const float* mel_in = a.mel + static_cast<size_t>(row) * 8 * kMelBins;
+    float* mp_in = a.mel_prev + (static_cast<size_t>(slot) * 2 + parity) * kMelBins;
+    float* mp_out = a.mel_prev + (static_cast<size_t>(slot) * 2 + (parity ^ 1)) * kMelBins;
+    // masked mel rows (row 0 = cached row), frequency-padded by one zero each side
+    for (int i = tid; i < 9 * 130; i += blockDim.x) {
+      const int r = i / 130, fq = i % 130 - 1;
+      float v = 0.0f;
+      if (fq >= 0 && fq < kMelBins) {
+        if (r == 0) {
+          v = mp_in[fq] * mel_prev_ok;
+        } else {
+          v = ((mask >> (r - 1)) & 1) ? mel_in[(r - 1) * kMelBins + fq] : 0.0f;
+        }
+      }
+      mels[i] = v;
+    }
+    // cached conv0 row -> conv1 input row 0
+    const __nv_bfloat16* sp_in =
+        a.sub_prev + (static_cast<size_t>(slot) * 2 + parity) * kF0 * 128;
+    for (int i = tid; i < kF0 * 64; i += blockDim.x) {  // 64 freq x 64 channel pairs
+      const int fq = i / 64, cp = i % 64;
+      __nv_bfloat162 v = reinterpret_cast<const __nv_bfloat162*>(sp_in)[fq * 64 + cp];
+      if (sub_prev_ok == 0.0f) v = __floats2bfloat162_rn(0.0f, 0.0f);
+      reinterpret_cast<__nv_bfloat162*>(xin + (0 * 66 + fq + 1) * kCiPad)[cp] = v;
+    }
+    __syncthreads();
+    // staged mel_prev = last mel row (unmasked)
+    for (int i = tid; i < kMelBins; i += blockDim.x) mp_out[i] = mel_in[7 * kMelBins + i];
+    // ---- conv0 + LN(128) + ReLU: warp -> 32 positions, lane -> 4 channels
+    __nv_bfloat16* sp_out = a.sub_prev + (static_cast<size_t>(slot) * 2 + (parity ^ 1)) * kF0 * 128;
+    float wr[4][9];
+#pragma unroll
+    for (int cc = 0; cc < 4; ++cc)
+#pragma unroll
+      for (int t = 0; t < 9; ++t) wr[cc][t] = w0s[(lane * 4 + cc) * 9 + t];
+    float g4[4];
+#pragma unroll
+    for (int cc = 0; cc < 4; ++cc) g4[cc] = ln0s[lane * 4 + cc];
+    for (int pi = 0; pi < 32; ++pi) {
+      const int p = warp * 32 + pi;  // 0..255
+      const int t = p >> 6, fq = p & 63;
+      float v[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int i = 0; i < 3; ++i)
+#pragma unroll
+        for (int j = 0; j < 3; ++j) {
+          const float xv = mels[(2 * t + i) * 130 + 2 * fq + j];  // padded index = freq + 1
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) v[cc] = fmaf(wr[cc][i * 3 + j], xv, v[cc]);
+        }
+      const float mean = warp_sum(v[0] + v[1] + v[2] + v[3]) * (1.0f / 128.0f);
+      float var = 0.f;
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) var += (v[cc] - mean) * (v[cc] - mean);
+      var = warp_sum(var) * (1.0f / 128.0f);
+      const float rstd = rsqrtf(var + a.eps);
+      const float keep = ((mask >> (2 * t)) & 1) ? 1.0f : 0.0f;  // mask0 = mask[::2]
+      __nv_bfloat16 o[4];
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        const float y = fmaxf((v[cc] - mean) * rstd * g4[cc], 0.0f);
+        o[cc] = __float2bfloat16_rn(y);
+      }
+      __nv_bfloat16 om[4];
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) om[cc] = __float2bfloat16_rn(__bfloat162float(o[cc]) * keep);
+      *reinterpret_cast<uint2*>(xin + ((1 + t) * 66 + fq + 1) * kCiPad + lane * 4) =
+          *reinterpret_cast<uint2*>(om);
+      if (t == 3) *reinterpret_cast<uint2*>(sp_out + fq * 128 + lane * 4) = *reinterpret_cast<uint2*>(o);
+    }
+    __syncthreads();
+    // ---- conv1 as implicit GEMM on mma.sync: D[pos][co] = sum_k A[pos][k] W1[co][k]
+    {
+      const int pt = warp & 3;          // position tile: 16 positions
+      const int ch = warp >> 2;         // channel half: 16 channels = 2 n-tiles
+      const int g = lane >> 2, tq = lane & 3;
+      float acc[2][4];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
+      const int p_lo = pt * 16 + g, p_hi = p_lo + 8;
+      const int t_lo = p_lo >> 5, f_lo = p_lo & 31, t_hi = p_hi >> 5, f_hi = p_hi & 31;
+      for (int ks = 0; ks < kK1 / 16; ++ks) {
+        const int tap = ks >> 3, ci0 = (ks & 7) * 16;
+        const int i = tap / 3, j = tap % 3;
+        const __nv_bfloat16* rlo = xin + ((2 * t_lo + i) * 66 + 2 * f_lo + j) * kCiPad + ci0;
+        const __nv_bfloat16* rhi = xin + ((2 * t_hi + i) * 66 + 2 * f_hi + j) * kCiPad + ci0;
+        uint32_t af[4];
+        af[0] = *reinterpret_cast<const uint32_t*>(rlo + 2 * tq);
+        af[1] = *reinterpret_cast<const uint32_t*>(rhi + 2 * tq);
+        af[2] = *reinterpret_cast<const uint32_t*>(rlo + 2 * tq + 8);
+        af[3] = *reinterpret_cast<const uint32_t*>(rhi + 2 * tq + 8);
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          const int co = ch * 16 + nt * 8 + g;
+          const __nv_bfloat16* wb = w1s + co * kK1Pad + ks * 16;
+          const uint32_t b0 = *reinterpret_cast<const uint32_t*>(wb + 2 * tq);
+          const uint32_t b1 = *reinterpret_cast<const uint32_t*>(wb + 2 * tq + 8);
+          mma_bf16_16816(acc[nt], af, b0, b1);
+        }
+      }
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        const int co = ch * 16 + nt * 8 + 2 * tq;
+        c1out[p_lo * 33 + co] = acc[nt][0];
+        c1out[p_lo * 33 + co + 1] = acc[nt][1];
+        c1out[p_hi * 33 + co] = acc[nt][2];
+        c1out[p_hi * 33 + co + 1] = acc[nt][3];
+      }
+    }
+    __syncthreads();
+    // ---- LN(C1) + ReLU, write [token t][f * C1 + c] bf16
+    if (tid < 64) {
+      const int p = tid, t = p >> 5, fq = p & 31;
+      float mean = 0.f;
+      for (int c = 0; c < 32; ++c) mean += c1out[p * 33 + c];
+      mean *= (1.0f / 32.0f);
+      float var = 0.f;
+      for (int c = 0; c < 32; ++c) {
+        const float dv = c1out[p * 33 + c] - mean;
+        var += dv * dv;
+      }
+      const float rstd = rsqrtf(var * (1.0f / 32.0f) + a.eps);
+      __nv_bfloat16* o = a.sub_in + (static_cast<size_t>(row) * 2 + t) * (32 * 32) + fq * 32;
+      for (int c = 0; c < 32; c += 2) {
+        const float y0 = fmaxf((c1out[p * 33 + c] - mean) * rstd * a.ln1[c], 0.f);
+        const float y1 = fmaxf((c1out[p * 33 + c + 1] - mean) * rstd * a.ln1[c + 1], 0.f);
+        *reinterpret_cast<__nv_bfloat162*>(o + c) = __floats2bfloat162_rn(y0, y1);
+      }
+    }
+  }
+}
+
+constexpr size_t kSubSmem = 128 + 32 * kK1Pad * 2 + 5 * 66 * kCiPad * 2 + 128 * 9 * 4 + 128 * 4 +
+                            9 * 130 * 4 + 64 * 33 * 4;
+
+}  // namespace
+
+cudaError_t launch_mel(Ctx& c, int rows_cap, int input_kind, cudaStream_t s) {
+  if (input_kind != LB_INPUT_PCM) return cudaSuccess;  // mel supplied by the caller
+  MelArgs a;
+  a.counts = c.dev_counts;
+  a.row_slot = c.row_slot;
+  a.row_reason = c.row_reason;
+  a.row_meta = c.row_meta;
+  a.pcm = c.in_pcm;
+  a.tail = c.pcm_tail;
+  a.mel = c.in_mel;
+  a.window = c.fe_window;
+  a.cos_tab = c.fe_cos;
+  a.sin_tab = c.fe_sin;
+  a.filters = c.fe_filters;
+  a.filter_range = c.fe_range;
+  mel_kernel<<<rows_cap, 256, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t frontend_init_attributes() {
+  return cudaFuncSetAttribute(subsample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              static_cast<int>(kSubSmem));
+}
+
+cudaError_t launch_subsample(Ctx& c, int rows_cap, cudaStream_t s) {
+  SubArgs a;
+  a.counts = c.dev_counts;
+  a.row_slot = c.row_slot;
+  a.row_mask = c.row_mask;
+  a.row_meta = c.row_meta;
+  a.mel = c.in_mel;
+  a.mel_prev = c.mel_prev;
+  a.sub_prev = c.sub_prev;
+  a.w0 = c.w.conv0;
+  a.ln0 = c.w.ln0;
+  a.w1 = c.w.conv1;
+  a.ln1 = c.w.ln1;
+  a.sub_in = c.sub_in;
+  a.eps = c.cfg.rms_eps;
+  a.c1 = c.cfg.sub_ch1;
+  int grid = rows_cap < c.num_sms ? rows_cap : c.num_sms;
+  subsample_kernel<<<grid, kSubThreads, kSubSmem, s>>>(a);
+  return cudaGetLastError();
+}
+
+size_t subsample_smem_bytes() { return kSubSmem; }
+
+}  // namespace lb

@@ -1,0 +1,600 @@
+// Per-layer non-GEMM kernels of the streaming Conformer step.
+//
+// All of them are row-parallel over the packed tokens (token 2r+t = tick token
+// t of batch row r), read the device row count and exit for rows beyond it, use
+// 16/32-byte vector loads and warp-shuffle reductions, and keep the residual
+// stream in fp32.
+//
+//   row_fused_kernel   FFN post-norm + 0.5-scaled residual, attention post-norm
+//                      + residual, norm_out, and the RMSNorm that produces the
+//                      next GEMM's bf16 input, in one pass
+//                      (transformers modeling_gemma4.py:390-408, 513-537;
+//                      streaming_conformer.py:777, 853-860)
+//   attention_kernel   chunked local attention of the 2 new tokens over each
+//                      session's K/V ring read in place: content + relative-
+//                      position logits, 50-softcap, window/validity mask,
+//                      fp32 softmax, weighted V; stages the 2 new K/V entries
+//                      (streaming_conformer.py:778-829, modeling_gemma4.py:209-314)
+//   lconv_kernel       GLU -> causal depthwise conv (k=5) over the conv-state
+//                      ring -> clamp -> RMSNorm -> SiLU -> bf16; stages the 2 new
+//                      GLU rows (streaming_conformer.py:830-852, modeling_gemma4.py:444-482)
+//   finalize_wide      split-K accumulator -> (SiLU) -> bf16
+//   outputs / film     output_proj + embed_audio tails and the FiLM elementwise
+//                      stages (streaming_conformer.py:871-872,
+//                      frame_residual_adapter.py:203-234)
+#include "common.cuh"
+#include "listener.h"
+
+#include <cmath>
+
+namespace lb {
+namespace {
+
+// Block-wide sum for blocks of up to 32 warps.
+__device__ __forceinline__ float block_sum(float v, float* sh) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) sh[warp] = v;
+  __syncthreads();
+  float t = 0.f;
+  for (int i = 0; i < nw; ++i) t += sh[i];
+  return t;
+}
+
+__device__ __forceinline__ void load8(const float* p, float (&v)[8]) {
+  const float4 a = reinterpret_cast<const float4*>(p)[0];
+  const float4 b = reinterpret_cast<const float4*>(p)[1];
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+__device__ __forceinline__ void store8(float* p, const float (&v)[8]) {
+  reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+  reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+}
+__device__ __forceinline__ void load8_bf16(const __nv_bfloat16* p, float (&v)[8]) {
+  const int4 r = *reinterpret_cast<const int4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&r);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void store8_bf16(__nv_bfloat16* p, const float (&v)[8]) {
+  int4 r;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&r);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+  *reinterpret_cast<int4*>(p) = r;
+}
+
+// RMSNorm of 8-element thread slices over a block row: x * pow(mean(x^2)+eps, -0.5) * w
+__device__ __forceinline__ void rms8(float (&v)[8], const float* w, int e0, int d, float eps,
+                                     float* sh) {
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) ss += v[i] * v[i];
+  ss = block_sum(ss, sh);
+  const float r = rsqrtf(ss / static_cast<float>(d) + eps);
+  if (w) {
+    float wv[8];
+    load8(w + e0, wv);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = v[i] * r * wv[i];
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = v[i] * r;
+  }
+}
+
+struct RowFusedDev {
+  const int* counts;
+  int d;
+  float eps, clip;
+  float* h;
+  const float* y;
+  const float* post_w;
+  float alpha;
+  int residual;
+  const float* out_w;
+  const float* pre_w;
+  int pre_norm, pre_clamp;
+  float in_lo, in_hi;
+  __nv_bfloat16* xa;
+  float* dbg;
+};
+
+__global__ void __launch_bounds__(256) row_fused_kernel(RowFusedDev a) {
+  __shared__ float sh[32];
+  const int t = blockIdx.x;
+  if (t >= a.counts[1]) return;
+  const int e0 = threadIdx.x * 8;
+  const size_t base = static_cast<size_t>(t) * a.d + e0;
+  float hv[8];
+  load8(a.h + base, hv);
+  if (a.y) {
+    float yv[8];
+    load8(a.y + base, yv);
+    if (a.post_w) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) yv[i] = fminf(fmaxf(yv[i], -a.clip), a.clip);
+      rms8(yv, a.post_w, e0, a.d, a.eps, sh);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) hv[i] = a.residual ? fmaf(yv[i], a.alpha, hv[i]) : yv[i] * a.alpha;
+  }
+  if (a.out_w) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) hv[i] = fminf(fmaxf(hv[i], -a.clip), a.clip);
+    rms8(hv, a.out_w, e0, a.d, a.eps, sh);
+  }
+  store8(a.h + base, hv);
+  if (a.dbg) store8(a.dbg + base, hv);
+  if (a.xa) {
+    float xv[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) xv[i] = a.pre_clamp ? fminf(fmaxf(hv[i], -a.clip), a.clip) : hv[i];
+    if (a.pre_norm) rms8(xv, a.pre_w, e0, a.d, a.eps, sh);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) xv[i] = fminf(fmaxf(xv[i], a.in_lo), a.in_hi);
+    store8_bf16(a.xa + base, xv);
+  }
+}
+
+// ------------------------------------------------------------- attention
+struct AttnDev {
+  const int* counts;
+  const int *row_slot, *row_mask;
+  const SlotMeta* row_meta;
+  const __nv_bfloat16* qkv;  // [tok][3d]
+  __nv_bfloat16 *kc, *vc;    // [S][L][16][d]
+  __nv_bfloat16* out;        // [tok][d]
+  const float* q_mult;       // [hd]
+  const float* rel;          // [13][d]
+  int layer, layers, d, hd;
+  float k_scale, softcap, invalid;
+  float in_lo, in_hi;  // attention.post input clamp
+};
+
+// One CTA per batch row, one warp per head.  Each lane owns head-dim pairs
+// e = 2*lane + 64*r (r < hd/64).
+template <int NP>  // NP = hd / 64 pairs per lane
+__global__ void __launch_bounds__(512) attention_kernel(AttnDev a) {
+  const int row = blockIdx.x;
+  if (row >= a.counts[0]) return;
+  const int head = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int slot = a.row_slot[row];
+  const SlotMeta m = a.row_meta[row];
+  const int mask = a.row_mask[row];
+  const int d = a.d;
+  const size_t ring_base = (static_cast<size_t>(slot) * a.layers + a.layer) * kRing * d;
+  const int hoff = head * a.hd;
+
+  float q[2][2 * NP], kn[2][2 * NP], vn[2][2 * NP], qm[2 * NP];
+#pragma unroll
+  for (int r = 0; r < NP; ++r) {
+    const int e = 2 * lane + 64 * r;
+    qm[2 * r] = a.q_mult[e];
+    qm[2 * r + 1] = a.q_mult[e + 1];
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      const __nv_bfloat16* src = a.qkv + (static_cast<size_t>(row) * 2 + t) * 3 * d + hoff + e;
+      const float2 qv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src));
+      const float2 kv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src + d));
+      const float2 vv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src + 2 * d));
+      q[t][2 * r] = qv.x * qm[2 * r];
+      q[t][2 * r + 1] = qv.y * qm[2 * r + 1];
+      kn[t][2 * r] = kv.x;
+      kn[t][2 * r + 1] = kv.y;
+      vn[t][2 * r] = vv.x;
+      vn[t][2 * r + 1] = vv.y;
+    }
+  }
+  // logits over 15 keys: j < 13 cached (ring entry pos + j), j = 13, 14 the new tokens
+  float logit[2][15];
+  const int first_real = kCached - m.fill;  // cached entries before this were never written
+  for (int j = 0; j < 15; ++j) {
+    float kv[2 * NP];
+    if (j < kCached) {
+      const int idx = (m.pos + j) & (kRing - 1);
+      const __nv_bfloat16* src = a.kc + ring_base + static_cast<size_t>(idx) * d + hoff;
+#pragma unroll
+      for (int r = 0; r < NP; ++r) {
+        float2 f = make_float2(0.f, 0.f);
+        if (j >= first_real)
+          f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src + 2 * lane + 64 * r));
+        kv[2 * r] = f.x;
+        kv[2 * r + 1] = f.y;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 2 * NP; ++i) kv[i] = kn[j - kCached][i];
+    }
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      const int dist = j < kCached ? (kCached - j + t) : (t - (j - kCached));
+      const int ridx = 12 - min(max(dist, 0), 12);
+      const float* rel = a.rel + static_cast<size_t>(ridx) * d + hoff;
+      float acc = 0.f;
+#pragma unroll
+      for (int r = 0; r < NP; ++r) {
+        const int e = 2 * lane + 64 * r;
+        acc = fmaf(q[t][2 * r], fmaf(kv[2 * r], a.k_scale, 0.f) + rel[e], acc);
+        acc = fmaf(q[t][2 * r + 1], fmaf(kv[2 * r + 1], a.k_scale, 0.f) + rel[e + 1], acc);
+      }
+      logit[t][j] = warp_sum(acc);
+    }
+  }
+  // softcap, mask, softmax (fp32), then weighted values
+  float p[2][15];
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    float mx = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 15; ++j) {
+      const int dist = j < kCached ? (kCached - j + t) : (t - (j - kCached));
+      bool ok = dist >= 0 && dist < 12;
+      if (j < kCached) {
+        ok = ok && ((m.valid_bits >> ((m.pos + j) & (kRing - 1))) & 1);
+      } else {
+        ok = ok && ((mask >> (4 * (j - kCached))) & 1);
+      }
+      float l = tanhf(logit[t][j] / a.softcap) * a.softcap;
+      l = ok ? l : a.invalid;
+      p[t][j] = l;
+      mx = fmaxf(mx, l);
+    }
+    float sum = 0.f;
+#pragma unroll
+    for (int j = 0; j < 15; ++j) {
+      p[t][j] = expf(p[t][j] - mx);
+      sum += p[t][j];
+    }
+    const float inv = 1.0f / sum;
+#pragma unroll
+    for (int j = 0; j < 15; ++j) p[t][j] *= inv;
+  }
+  float o[2][2 * NP];
+#pragma unroll
+  for (int t = 0; t < 2; ++t)
+#pragma unroll
+    for (int i = 0; i < 2 * NP; ++i) o[t][i] = 0.f;
+  for (int j = 0; j < 15; ++j) {
+    float vv[2 * NP];
+    if (j < kCached) {
+      const int idx = (m.pos + j) & (kRing - 1);
+      const __nv_bfloat16* src = a.vc + ring_base + static_cast<size_t>(idx) * d + hoff;
+      const bool live = j >= first_real && (p[0][j] != 0.f || p[1][j] != 0.f);
+#pragma unroll
+      for (int r = 0; r < NP; ++r) {
+        float2 f = make_float2(0.f, 0.f);
+        if (live)
+          f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src + 2 * lane + 64 * r));
+        vv[2 * r] = f.x;
+        vv[2 * r + 1] = f.y;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 2 * NP; ++i) vv[i] = vn[j - kCached][i];
+    }
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+      for (int i = 0; i < 2 * NP; ++i) o[t][i] = fmaf(p[t][j], vv[i], o[t][i]);
+  }
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    __nv_bfloat16* dst = a.out + (static_cast<size_t>(row) * 2 + t) * d + hoff;
+#pragma unroll
+    for (int r = 0; r < NP; ++r)
+      *reinterpret_cast<__nv_bfloat162*>(dst + 2 * lane + 64 * r) =
+          __floats2bfloat162_rn(fminf(fmaxf(o[t][2 * r], a.in_lo), a.in_hi),
+                                fminf(fmaxf(o[t][2 * r + 1], a.in_lo), a.in_hi));
+  }
+  // stage the two new K/V entries at ring positions pos+13, pos+14
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const int idx = (m.pos + kCached + t) & (kRing - 1);
+    __nv_bfloat16* kd = a.kc + ring_base + static_cast<size_t>(idx) * d + hoff;
+    __nv_bfloat16* vd = a.vc + ring_base + static_cast<size_t>(idx) * d + hoff;
+#pragma unroll
+    for (int r = 0; r < NP; ++r) {
+      const int e = 2 * lane + 64 * r;
+      *reinterpret_cast<__nv_bfloat162*>(kd + e) = __floats2bfloat162_rn(kn[t][2 * r], kn[t][2 * r + 1]);
+      *reinterpret_cast<__nv_bfloat162*>(vd + e) = __floats2bfloat162_rn(vn[t][2 * r], vn[t][2 * r + 1]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------- lconv
+struct LconvDev {
+  const int* counts;
+  const int* row_slot;
+  const SlotMeta* row_meta;
+  const __nv_bfloat16* gl;   // [tok][2d]
+  __nv_bfloat16* ring;       // [S][L][8][d]
+  const float* dw;           // [d][5]
+  const float* norm_w;       // [d]
+  __nv_bfloat16* xa;         // [tok][d]
+  int layer, layers, d;
+  float eps, clip, in_lo, in_hi;
+};
+
+__global__ void __launch_bounds__(256) lconv_kernel(LconvDev a) {
+  __shared__ float sh[32];
+  const int row = blockIdx.x;
+  if (row >= a.counts[0]) return;
+  const int d = a.d;
+  const int e0 = threadIdx.x * 8;
+  const int slot = a.row_slot[row];
+  const SlotMeta m = a.row_meta[row];
+  const size_t rb = (static_cast<size_t>(slot) * a.layers + a.layer) * kConvRing * d;
+  float win[6][8];
+  const int first_real = 4 - min(m.fill, 4);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    if (j >= first_real) {
+      load8_bf16(a.ring + rb + static_cast<size_t>((m.pos + j) & (kConvRing - 1)) * d + e0, win[j]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) win[j][i] = 0.f;
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    float av[8], bv[8];
+    const __nv_bfloat16* g = a.gl + (static_cast<size_t>(row) * 2 + t) * 2 * d;
+    load8_bf16(g + e0, av);
+    load8_bf16(g + d + e0, bv);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) win[4 + t][i] = bf16_round(av[i] / (1.0f + expf(-bv[i])));
+    store8_bf16(a.ring + rb + static_cast<size_t>((m.pos + 4 + t) & (kConvRing - 1)) * d + e0,
+                win[4 + t]);
+  }
+  float w5[8][5];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int k = 0; k < 5; ++k) w5[i][k] = a.dw[(e0 + i) * 5 + k];
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    float cv[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float acc = 0.f;
+#pragma unroll
+      for (int k = 0; k < 5; ++k) acc = fmaf(w5[i][k], win[t + k][i], acc);
+      cv[i] = fminf(fmaxf(acc, -a.clip), a.clip);
+    }
+    rms8(cv, a.norm_w, e0, d, a.eps, sh);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) cv[i] = fminf(fmaxf(silu_f(cv[i]), a.in_lo), a.in_hi);
+    store8_bf16(a.xa + (static_cast<size_t>(row) * 2 + t) * d + e0, cv);
+  }
+}
+
+// ------------------------------------------------------- split-K finalize
+__global__ void finalize_wide_kernel(const int* counts, const float* acc, int width, int act,
+                                     __nv_bfloat16* out, float lo, float hi, float plo, float phi) {
+  const int t = blockIdx.y;
+  if (t >= counts[1]) return;
+  const int o = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (o >= width) return;
+  float v[8];
+  load8(acc + static_cast<size_t>(t) * width + o, v);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float y = fminf(fmaxf(v[i], lo), hi);
+    if (act == 1) y = silu_f(bf16_round(y));
+    v[i] = fminf(fmaxf(y, plo), phi);
+  }
+  store8_bf16(out + static_cast<size_t>(t) * width + o, v);
+}
+
+// ----------------------------------------------------------- output tails
+// stage 0: y = output_proj(h) fp32 -> raw bf16, embed input bf16(RMS(raw)) (no scale)
+// stage 1: y = embed(...) fp32 -> soft bf16
+__global__ void __launch_bounds__(256) outputs_kernel(const int* counts, const float* y, int width,
+                                                     int stage, __nv_bfloat16* out,
+                                                     __nv_bfloat16* next_in, float eps) {
+  __shared__ float sh[32];
+  const int t = blockIdx.x;
+  if (t >= counts[1]) return;
+  const int e0 = threadIdx.x * 8;
+  float v[8];
+  load8(y + static_cast<size_t>(t) * width + e0, v);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = bf16_round(v[i]);
+  store8_bf16(out + static_cast<size_t>(t) * width + e0, v);
+  if (stage == 0) {
+    rms8(v, nullptr, e0, width, eps, sh);
+    store8_bf16(next_in + static_cast<size_t>(t) * width + e0, v);
+  }
+}
+
+// FiLM stage 0: LayerNorm(query) and LayerNorm(soft) -> bf16 GEMM inputs, RMS(query) -> amp
+__global__ void __launch_bounds__(256) film_norm_kernel(const int* counts, const __nv_bfloat16* query,
+                                                       int qdim, const __nv_bfloat16* soft, int hdim,
+                                                       const float* qw, const float* qb,
+                                                       const float* hw, const float* hb,
+                                                       __nv_bfloat16* xq, __nv_bfloat16* xr,
+                                                       float* amp) {
+  __shared__ float sh[32];
+  const int t = blockIdx.x;
+  if (t >= counts[1]) return;
+  for (int pass = 0; pass < 2; ++pass) {
+    const int dim = pass == 0 ? qdim : hdim;
+    const __nv_bfloat16* src = (pass == 0 ? query : soft) + static_cast<size_t>(t) * dim;
+    const float* w = pass == 0 ? qw : hw;
+    const float* b = pass == 0 ? qb : hb;
+    __nv_bfloat16* dst = (pass == 0 ? xq : xr) + static_cast<size_t>(t) * dim;
+    float s = 0.f, ss = 0.f;
+    for (int e = threadIdx.x * 8; e < dim; e += blockDim.x * 8) {
+      float v[8];
+      load8_bf16(src + e, v);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        s += v[i];
+        ss += v[i] * v[i];
+      }
+    }
+    s = block_sum(s, sh);
+    ss = block_sum(ss, sh);
+    const float mean = s / dim;
+    const float var = fmaxf(ss / dim - mean * mean, 0.f);
+    const float rstd = rsqrtf(var + 1e-5f);
+    if (pass == 0 && threadIdx.x == 0) amp[t] = sqrtf(ss / dim);
+    for (int e = threadIdx.x * 8; e < dim; e += blockDim.x * 8) {
+      float v[8], wv[8], bv[8];
+      load8_bf16(src + e, v);
+      load8(w + e, wv);
+      load8(b + e, bv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = (v[i] - mean) * rstd * wv[i] + bv[i];
+      store8_bf16(dst + e, v);
+    }
+  }
+}
+
+// FiLM stage 1: fused = SiLU(qd * (1 + tanh(gamma)) + beta) -> bf16
+__global__ void film_fuse_kernel(const int* counts, const float* qd, const float* gb, int bdim,
+                                 __nv_bfloat16* fused) {
+  const int t = blockIdx.x;
+  if (t >= counts[1]) return;
+  for (int e = threadIdx.x; e < bdim; e += blockDim.x) {
+    const float g = gb[static_cast<size_t>(t) * 2 * bdim + e];
+    const float b = gb[static_cast<size_t>(t) * 2 * bdim + bdim + e];
+    const float v = qd[static_cast<size_t>(t) * bdim + e] * (1.0f + tanhf(g)) + b;
+    fused[static_cast<size_t>(t) * bdim + e] = __float2bfloat16_rn(silu_f(v));
+  }
+}
+
+// FiLM stage 2: out = query + tanh(mapped) * scale * RMS(query)
+__global__ void film_out_kernel(const int* counts, const float* mapped, const __nv_bfloat16* query,
+                                const float* amp, int qdim, float scale, __nv_bfloat16* out) {
+  const int t = blockIdx.y;
+  if (t >= counts[1]) return;
+  const int e = blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= qdim) return;
+  const size_t i = static_cast<size_t>(t) * qdim + e;
+  const float r = tanhf(mapped[i]) * scale * amp[t];
+  out[i] = __float2bfloat16_rn(__bfloat162float(query[i]) + r);
+}
+
+}  // namespace
+
+cudaError_t launch_row_fused(Ctx& c, int tok_cap, const RowFusedArgs& r, cudaStream_t s) {
+  RowFusedDev a;
+  a.counts = c.dev_counts;
+  a.d = c.cfg.hidden;
+  a.eps = c.cfg.rms_eps;
+  a.clip = c.cfg.gradient_clipping;
+  a.h = c.h;
+  a.y = r.y;
+  a.post_w = r.post_w;
+  a.alpha = r.alpha;
+  a.residual = r.residual ? 1 : 0;
+  a.out_w = r.out_w;
+  a.pre_w = r.pre_w;
+  a.pre_norm = r.pre_norm ? 1 : 0;
+  a.pre_clamp = r.pre_clamp ? 1 : 0;
+  a.in_lo = r.in_lo;
+  a.in_hi = r.in_hi;
+  a.xa = r.xa;
+  a.dbg = r.dbg;
+  row_fused_kernel<<<tok_cap, c.cfg.hidden / 8, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_attention(Ctx& c, int layer, int rows_cap, cudaStream_t s) {
+  AttnDev a;
+  a.counts = c.dev_counts;
+  a.row_slot = c.row_slot;
+  a.row_mask = c.row_mask;
+  a.row_meta = c.row_meta;
+  a.qkv = c.qkv;
+  a.kc = c.kv_k;
+  a.vc = c.kv_v;
+  a.out = c.att;
+  a.q_mult = c.w.layers[layer].q_mult;
+  a.rel = c.w.layers[layer].rel_keys;
+  a.layer = layer;
+  a.layers = c.cfg.layers;
+  a.d = c.cfg.hidden;
+  a.hd = c.hd;
+  a.k_scale = static_cast<float>(std::log1p(std::exp(1.0)) / std::log(2.0));
+  a.softcap = c.cfg.softcap;
+  a.invalid = c.cfg.invalid_logit;
+  a.in_lo = c.w.layers[layer].clip[5][0];
+  a.in_hi = c.w.layers[layer].clip[5][1];
+  const int threads = 32 * c.cfg.heads;
+  switch (c.hd / 64) {
+    case 1: attention_kernel<1><<<rows_cap, threads, 0, s>>>(a); break;
+    case 2: attention_kernel<2><<<rows_cap, threads, 0, s>>>(a); break;
+    case 3: attention_kernel<3><<<rows_cap, threads, 0, s>>>(a); break;
+    case 4: attention_kernel<4><<<rows_cap, threads, 0, s>>>(a); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_lconv(Ctx& c, int layer, int rows_cap, cudaStream_t s) {
+  LconvDev a;
+  a.counts = c.dev_counts;
+  a.row_slot = c.row_slot;
+  a.row_meta = c.row_meta;
+  a.gl = c.gl;
+  a.ring = c.conv_ring;
+  a.dw = c.w.layers[layer].lc_dw;
+  a.norm_w = c.w.layers[layer].lc_norm;
+  a.xa = c.xa;
+  a.layer = layer;
+  a.layers = c.cfg.layers;
+  a.d = c.cfg.hidden;
+  a.eps = c.cfg.rms_eps;
+  a.clip = c.cfg.gradient_clipping;
+  a.in_lo = c.w.layers[layer].clip[7][0];  // linear_end input bounds
+  a.in_hi = c.w.layers[layer].clip[7][1];
+  lconv_kernel<<<rows_cap, c.cfg.hidden / 8, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_finalize_wide(Ctx& c, int tok_cap, const float* acc, int width, int act,
+                                 __nv_bfloat16* out, const float* out_clip, cudaStream_t s) {
+  const int per_block = 128 * 8;
+  dim3 grid((width + per_block - 1) / per_block, tok_cap);
+  finalize_wide_kernel<<<grid, 128, 0, s>>>(c.dev_counts, acc, width, act, out,
+                                            out_clip ? out_clip[0] : -INFINITY,
+                                            out_clip ? out_clip[1] : INFINITY,
+                                            out_clip ? out_clip[2] : -INFINITY,
+                                            out_clip ? out_clip[3] : INFINITY);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_outputs(Ctx& c, int tok_cap, int stage, cudaStream_t s) {
+  const int width = stage == 0 ? c.cfg.output_dims : c.cfg.text_hidden;
+  outputs_kernel<<<tok_cap, width / 8, 0, s>>>(c.dev_counts, c.y, width, stage,
+                                               stage == 0 ? c.out_raw : c.out_soft, c.xe,
+                                               c.cfg.rms_eps);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_film(Ctx& c, int tok_cap, int stage, cudaStream_t s) {
+  const int Q = c.cfg.film_query_dim, B = c.cfg.film_bottleneck, T = c.cfg.text_hidden;
+  if (stage == 0) {
+    film_norm_kernel<<<tok_cap, 128, 0, s>>>(c.dev_counts, c.in_query, Q, c.out_soft, T,
+                                             c.w.fq_norm_w, c.w.fq_norm_b, c.w.fr_norm_w,
+                                             c.w.fr_norm_b, c.film_xq, c.film_xr, c.film_amp);
+  } else if (stage == 1) {
+    film_fuse_kernel<<<tok_cap, 128, 0, s>>>(c.dev_counts, c.film_qd, c.film_gb, B, c.film_fused);
+  } else {
+    dim3 grid((Q + 255) / 256, tok_cap);
+    film_out_kernel<<<grid, 256, 0, s>>>(c.dev_counts, c.film_map, c.in_query, c.film_amp, Q,
+                                         c.w.film_scale, c.out_film);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace lb

@@ -1,0 +1,51 @@
+// Internal (host-side) interface between the C-ABI layer and the kernels.
+// Nothing here is exported; the public surface is include/listener_b200.h.
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+
+namespace lb {
+
+// ------------------------------------------------------------------ GEMM
+struct GemmParams {
+  int K = 0;                   // reduction length (multiple of 64)
+  int O = 0;                   // output features (multiple of 128)
+  const int* m_dev = nullptr;  // device token count; null -> m_static
+  int m_static = 0;
+  int kb_per_split = 0;
+  const __half* w_scale = nullptr;  // per-output-channel scale (int8 weights)
+  const float* bias = nullptr;      // per-output-channel bias (fp32) or null
+  void* out = nullptr;
+  int ld_out = 0;    // elements between consecutive token rows of `out`
+  int out_mode = 0;  // 0: bf16 store, 1: fp32 store, 2: fp32 atomic add (split-K)
+  int act = 0;       // 0: none, 1: SiLU of the bf16-rounded linear output
+  float out_lo = -INFINITY, out_hi = INFINITY;    // linear output clamp (before act)
+  float post_lo = -INFINITY, post_hi = INFINITY;  // next linear's input clamp (after act)
+  int* status = nullptr;
+};
+
+struct GemmPlan {
+  CUtensorMap tm_w;
+  CUtensorMap tm_x;
+  int O = 0, K = 0, m_cap = 0, tn = 0;
+  bool w_int8 = false;
+};
+
+int make_tensor_map_2d(CUtensorMap* map, const void* base, int elem_bytes, uint64_t inner,
+                       uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
+                       uint32_t box_outer, bool swizzle128);
+int gemm_token_tile(int m_cap);
+// Encodes the tensor maps for W ([O,K] bf16 or int8) and X ([m_cap,K], row
+// stride x_ld elements).  X needs m_cap rows; TMA zero-fills the rest.
+int gemm_prepare(GemmPlan* plan, const void* w, bool w_int8, int O, int K, const void* x, int x_ld,
+                 int m_cap);
+cudaError_t gemm_launch(const GemmPlan& plan, GemmParams p, int splits, cudaStream_t stream);
+int gemm_pick_splits(const GemmPlan& plan, int num_sms);
+
+}  // namespace lb

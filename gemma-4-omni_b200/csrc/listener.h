@@ -1,0 +1,235 @@
+// Internal context of a listener step instance (one per GPU / process).
+//
+// Device memory layout (all owned by the context, allocated at lb_create):
+//
+//   weights   one arena; GEMM weights bf16 [O,K] or int8 [O,K] + fp16 scale[O];
+//             norms / conv / biases fp32 (bf16-rounded values).
+//   sessions  persistent per-slot state, S = max_sessions slots:
+//               kv_k, kv_v  bf16 [S][L][16][d]   ring of the last 13 projected
+//                           keys / values (pre-scale, exactly the bf16 linear
+//                           outputs) plus 2 staged + 1 spare entries
+//               conv_ring   bf16 [S][L][8][d]    ring of the last 4 GLU rows + 2 staged
+//               sub_prev    bf16 [S][2][128][64] last conv0 output row, double-buffered
+//               mel_prev    f32  [S][2][128]     last mel row, double-buffered
+//               pcm_tail    f32  [S][2][160]     last 160 PCM samples, double-buffered
+//               meta        int4 [S] x3          canonical / staged / rollback backup
+//                           {pos, fill, valid_bits, flags}
+//             A step writes only staged ring entries and the staged meta; commit
+//             copies staged meta -> canonical (the "ring head swap"), so no cache
+//             window is ever copied (reference: full-window index_copy_ staging,
+//             duplex_kernel/streaming_conformer.py:682-697, 904-958).
+//   tables    session-handle directory for the packer (handle -> slot / key /
+//             expected cursor) and slot -> owner.
+//   rows      per-step row tables written by the packer (row -> slot, reset,
+//             reason) and the device row count read by every kernel.
+//   acts      activation buffers sized for 2*max_rows tokens.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <map>
+#include <string>
+#include <vector>
+
+#include "../../include/listener_b200.h"
+#include "kernels.h"
+
+namespace lb {
+
+constexpr int kRing = 16;      // K/V ring entries per slot per layer
+constexpr int kConvRing = 8;   // conv-state ring entries
+constexpr int kCached = 13;    // CACHED_PAST_TOKENS
+constexpr int kMelBins = 128;
+constexpr int kPcm = 1280;
+constexpr int kTail = 160;
+
+struct SlotMeta {
+  int pos;         // ring base: canonical entries are (pos + j) mod ring
+  int fill;        // tokens written since the last reset (saturates at 13)
+  int valid_bits;  // token-valid bit per K/V ring entry
+  int flags;       // bit0: mel_prev valid, bit1: sub_prev valid
+};
+
+struct LayerW {
+  float *ffn_pre[2], *ffn_post[2];
+  void *w_ffn1[2], *w_ffn2[2];
+  __half *s_ffn1[2], *s_ffn2[2];
+  float *norm_pre_attn, *norm_post_attn, *norm_out;
+  void* w_qkv;
+  __half* s_qkv;
+  void* w_post;
+  __half* s_post;
+  float* q_mult;    // [hd] q_scale * softplus(per_dim_scale)
+  float* rel_keys;  // [13][d] relative keys, fp32
+  float *lc_pre, *lc_norm;
+  float* lc_dw;     // [d][5]
+  void *w_lstart, *w_lend;
+  __half *s_lstart, *s_lend;
+  float clip[8][4];  // per linear: in_lo, in_hi, out_lo, out_hi
+};
+
+struct Weights {
+  float* conv0;    // [128][9]
+  float* ln0;      // [128]
+  __nv_bfloat16* conv1;  // [C1][9*128 (+pad)] k = (i*3+j)*128 + ci
+  float* ln1;      // [C1]
+  void* w_in;
+  __half* s_in;
+  std::vector<LayerW> layers;
+  void* w_out;
+  __half* s_out;
+  float* b_out;
+  void* w_embed;
+  __half* s_embed;
+  // FiLM
+  float *fq_norm_w, *fq_norm_b, *fr_norm_w, *fr_norm_b;
+  void *w_qdown, *w_rdown, *w_film, *w_fout;
+  __half *s_qdown, *s_rdown, *s_film, *s_fout;
+  float *b_qdown, *b_rdown, *b_film, *b_fout;
+  float film_scale;  // 0.25 * sigmoid(scale_logit), set from the host
+};
+
+struct TensorSlot {
+  void* dst;
+  int dtype;
+  int64_t numel;
+  bool set = false;
+  bool gemm = false;  // GEMM weight (bf16, or int8 with ":scale" companion)
+  int qkv_part = -1;
+  float* clip_dst = nullptr;  // for clip bound scalars
+};
+
+struct Ctx;
+
+// One GEMM of the step at one token tile size.
+struct GemmOp {
+  GemmPlan plan;
+  GemmParams params;
+  int splits = 1;
+};
+
+struct Bucket {
+  int rows_cap = 0;   // sessions
+  int tok_cap = 0;    // 2 * rows_cap
+  cudaGraphExec_t graph = nullptr;
+  bool graph_ready = false;
+};
+
+struct Ctx {
+  lb_config cfg{};
+  int device = 0;
+  int num_sms = 148;
+  int hd = 0;
+  int weight_int8 = 0;
+
+  // arenas
+  void* weight_arena = nullptr;
+  size_t weight_bytes = 0;
+  void* state_arena = nullptr;
+  size_t state_bytes = 0;
+  void* act_arena = nullptr;
+  size_t act_bytes = 0;
+
+  Weights w{};
+  std::map<std::string, TensorSlot> tensors;
+  bool weights_final = false;
+
+  // persistent session state
+  __nv_bfloat16 *kv_k = nullptr, *kv_v = nullptr, *conv_ring = nullptr, *sub_prev = nullptr;
+  float *mel_prev = nullptr, *pcm_tail = nullptr;
+  SlotMeta *meta_canon = nullptr, *meta_stage = nullptr, *meta_backup = nullptr;
+  // handle directory
+  int max_handles = 0;
+  int *handle_slot = nullptr, *slot_owner = nullptr;
+  long long *handle_key = nullptr, *handle_exp_frame = nullptr, *handle_exp_seq = nullptr;
+  long long* handle_stamp = nullptr;
+  // rollback record of the last committed batch
+  int* bk_handle_slot = nullptr;
+  long long *bk_handle_key = nullptr, *bk_handle_exp_frame = nullptr, *bk_handle_exp_seq = nullptr;
+  int* bk_slot_owner = nullptr;  // previous owner of each committed row's slot
+  int* bk_prev_handle_slot = nullptr;
+  // per-step rows
+  int* dev_counts = nullptr;  // [0] n_rows, [1] n_tok, [2] committed rows, [3] packed flag
+  int* status = nullptr;      // device status word
+  int *row_handle = nullptr, *row_slot = nullptr, *row_reason = nullptr, *row_reset = nullptr;
+  int *row_mask = nullptr, *row_replacing = nullptr;
+  uint8_t* row_mask_in = nullptr;  // caller's uint8 masks (copied per step)
+  SlotMeta* row_meta = nullptr;    // effective canonical meta per row (reset applied)
+  long long *row_key = nullptr, *row_frame = nullptr, *row_seq = nullptr;
+  long long *row_exp_frame = nullptr, *row_exp_seq = nullptr;
+  int* free_list = nullptr;
+  long long step_id = 0;
+  int packed_rows = 0;  // host copy of the last pack's row count
+  int state = 0;        // 0 idle, 1 packed, 2 stepped, 3 committed(rollback-able)
+  int last_commit_rows = 0;
+
+  // activations [tok_cap]
+  float* in_pcm = nullptr;    // [rows][1280]
+  float* in_mel = nullptr;    // [rows][8][128]
+  __nv_bfloat16* in_query = nullptr;  // [tok][Q]
+  __nv_bfloat16* sub_in = nullptr;    // [tok][C1*F1]
+  float* h = nullptr;                 // [tok][d]
+  float* y = nullptr;                 // [tok][max(d, out, text)] narrow fp32 outputs
+  __nv_bfloat16* xa = nullptr;        // [tok][d]  GEMM input
+  __nv_bfloat16* xf = nullptr;        // [tok][F]  FFN mid
+  __nv_bfloat16* qkv = nullptr;       // [tok][3d]
+  __nv_bfloat16* att = nullptr;       // [tok][d]
+  __nv_bfloat16* gl = nullptr;        // [tok][2d] linear_start output
+  float* wide_acc = nullptr;          // [tok][max(F,3d,2d)] split-K accumulators
+  __nv_bfloat16* out_raw = nullptr;   // [tok][out]
+  __nv_bfloat16* out_soft = nullptr;  // [tok][text]
+  __nv_bfloat16* out_film = nullptr;  // [tok][Q]
+  __nv_bfloat16* film_xq = nullptr;   // [tok][Q] LN(query)
+  __nv_bfloat16* film_xr = nullptr;   // [tok][text] LN(soft)
+  float* film_qd = nullptr;           // [tok][B]
+  float* film_rd = nullptr;           // [tok][B]
+  __nv_bfloat16* film_rd_bf = nullptr;  // [tok][B]
+  float* film_gb = nullptr;           // [tok][2B]
+  __nv_bfloat16* film_fused = nullptr;  // [tok][B]
+  float* film_map = nullptr;          // [tok][Q]
+  float* film_amp = nullptr;          // [tok] RMS(query)
+  __nv_bfloat16* xe = nullptr;        // [tok][out] embedder input
+  // optional per-layer debug outputs (null in serving)
+  float* dbg_sub = nullptr;
+  float* dbg_layers = nullptr;
+
+  // frontend tables: periodic Hann window [320], DFT twiddles [512] x2,
+  // mel filterbank [257][128] and its non-zero row range per mel bin
+  float *fe_window = nullptr, *fe_cos = nullptr, *fe_sin = nullptr, *fe_filters = nullptr;
+  int2* fe_range = nullptr;
+
+  std::vector<Bucket> buckets;
+  cudaStream_t capture_stream = nullptr;
+};
+
+// --------------------------------------------------------- kernel launchers
+cudaError_t launch_mel(Ctx& c, int rows_cap, int input_kind, cudaStream_t s);
+cudaError_t launch_subsample(Ctx& c, int rows_cap, cudaStream_t s);
+cudaError_t launch_pack(Ctx& c, int n_rows, long long step_id, cudaStream_t s);
+cudaError_t launch_commit(Ctx& c, cudaStream_t s);
+cudaError_t launch_rollback(Ctx& c, cudaStream_t s);
+cudaError_t launch_reset(Ctx& c, int handle, int slot, cudaStream_t s);
+cudaError_t run_layers(Ctx& c, const Bucket& b, cudaStream_t s);
+
+struct RowFusedArgs {
+  const float* y = nullptr;   // GEMM fp32 output (or null: no addend)
+  const float* post_w = nullptr;  // RMSNorm weight applied to clamp(y) (null: none)
+  float alpha = 1.0f;
+  bool residual = true;           // h = alpha * post(y) + h   (else h = alpha * post(y))
+  const float* out_w = nullptr;   // norm_out RMSNorm of clamp(h) (null: none)
+  const float* pre_w = nullptr;   // RMSNorm weight for the next GEMM input
+  bool pre_norm = true;           // false: xa = bf16(h) without normalisation
+  bool pre_clamp = true;          // clamp(h, +/-clip) before the pre-norm
+  float in_lo = -INFINITY, in_hi = INFINITY;  // next linear's input clamp
+  __nv_bfloat16* xa = nullptr;
+  float* dbg = nullptr;           // optional copy of the new h
+};
+cudaError_t launch_row_fused(Ctx& c, int tok_cap, const RowFusedArgs& a, cudaStream_t s);
+cudaError_t launch_attention(Ctx& c, int layer, int rows_cap, cudaStream_t s);
+cudaError_t launch_lconv(Ctx& c, int layer, int rows_cap, cudaStream_t s);
+cudaError_t launch_finalize_wide(Ctx& c, int tok_cap, const float* acc, int width, int act,
+                                 __nv_bfloat16* out, const float* out_clip, cudaStream_t s);
+cudaError_t launch_outputs(Ctx& c, int tok_cap, int stage, cudaStream_t s);
+cudaError_t launch_film(Ctx& c, int tok_cap, int stage, cudaStream_t s);
+
+}  // namespace lb

@@ -1,0 +1,198 @@
+/*
+ * listener_b200.h — C ABI of the B200-native streaming listener step.
+ *
+ * One call of lb_step_async() runs, for every active session of a step, the
+ * reference's per-80 ms listener hot path:
+ *   PCM frame -> log-mel (duplex_kernel/listener.py:1807-1850)
+ *   -> causal chunked-attention Gemma 4 audio Conformer with per-session
+ *      K/V, conv and subsampler caches (duplex_kernel/streaming_conformer.py:700-888)
+ *   -> output_proj + embed_audio soft tokens (streaming_conformer.py:871-872)
+ *   -> optional FrameResidualQueryFiLM residual (duplex_kernel/frame_residual_adapter.py:203-237).
+ *
+ * Conventions (mirroring the reference's native batch ABI,
+ * native/gemma4_listener_microbatch/gemma4_listener_microbatch.h:206-480):
+ *   - every function returns an int status: 0 = ok, negative = error;
+ *   - configuration structs carry struct_size and api_version;
+ *   - contexts are opaque; all device work is enqueued on the caller's
+ *     cudaStream_t (passed as void*) and nothing synchronises the host except
+ *     lb_get_status / lb_read_* helpers, which say so;
+ *   - pointers are plain device pointers unless a name says "host".
+ */
+#ifndef LISTENER_B200_H_
+#define LISTENER_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LB_API_VERSION 1
+
+enum lb_status_code {
+  LB_OK = 0,
+  LB_ERR_INVALID_ARGUMENT = -1,
+  LB_ERR_CUDA = -2,
+  LB_ERR_STATE = -3,        /* call not valid in the context's current state */
+  LB_ERR_CAPACITY = -4,     /* session bank exhausted / size beyond capacity */
+  LB_ERR_VERSION = -5,      /* struct_size / api_version mismatch */
+  LB_ERR_DEVICE_STATUS = -6 /* device status word is non-zero (see lb_get_status) */
+};
+
+/* Device status bits reported by lb_get_status(). */
+enum lb_device_status_bits {
+  LB_DEV_WAIT_TIMEOUT = 1 << 0,
+  LB_DEV_SLOT_EXHAUSTED = 1 << 1,
+  LB_DEV_DUPLICATE_ROW = 1 << 2,
+  LB_DEV_BAD_HANDLE = 1 << 3,
+  LB_DEV_STALE_COMMIT = 1 << 4,
+  LB_DEV_BAD_ROW_COUNT = 1 << 5
+};
+
+/* Tensor element types for lb_set_tensor. */
+enum lb_dtype { LB_F32 = 0, LB_BF16 = 1, LB_I8 = 2, LB_F16 = 3 };
+
+/* Weight formats of the dense contractions. */
+enum lb_weight_format {
+  LB_WEIGHTS_BF16 = 0,
+  LB_WEIGHTS_INT8 = 1 /* int8 rows + one fp16 scale per output channel */
+};
+
+/* Step input kinds for lb_step_async. */
+enum lb_input_kind {
+  LB_INPUT_PCM = 0, /* float32 [n_rows][1280] 16 kHz PCM; log-mel runs on the GPU */
+  LB_INPUT_MEL = 1  /* float32 [n_rows][8][128] log-mel tick (tower-only form) */
+};
+
+/* Row reasons written by lb_pack_async (streaming_conformer.py:571-606). */
+enum lb_row_reason {
+  LB_REASON_CONTINUE = 0,
+  LB_REASON_RESET = 1,
+  LB_REASON_GAP_OR_CURSOR_MISMATCH = 2,
+  LB_REASON_IDENTITY_RESET = 3
+};
+
+/* Context configuration.  The model shape is that of transformers'
+ * Gemma4AudioConfig (models/gemma4/configuration_gemma4.py:27-80) plus the
+ * FiLM adapter (frame_residual_adapter.py:164-197). */
+typedef struct lb_config {
+  uint32_t struct_size; /* sizeof(lb_config) */
+  uint32_t api_version; /* LB_API_VERSION */
+  int32_t max_sessions; /* persistent cache slots (StreamingConformerAudioTower max_sessions) */
+  int32_t max_handles;  /* session-handle table size (>= max_sessions) */
+  int32_t max_rows;     /* largest batch of one step */
+  int32_t hidden, layers, heads, ffn;
+  int32_t sub_ch0, sub_ch1;
+  int32_t output_dims, text_hidden;
+  int32_t conv_kernel; /* must be 5 */
+  int32_t weight_format;
+  int32_t film_enabled;
+  int32_t film_query_dim, film_bottleneck;
+  float rms_eps, softcap, invalid_logit, gradient_clipping, residual_weight;
+  float film_max_scale;
+} lb_config;
+
+typedef struct lb_ctx lb_ctx;
+
+/* Creates a context on the current CUDA device: allocates the weight arena,
+ * the per-slot session state (zeroed) and the activation buffers.
+ * Replaces StreamingConformerAudioTower.__init__ (streaming_conformer.py:138-294)
+ * and the native batch create call (gemma4_listener_microbatch.h). */
+int lb_create(const lb_config* cfg, lb_ctx** out_ctx);
+int lb_destroy(lb_ctx* ctx);
+
+/* Uploads one named parameter (transformers Gemma4AudioModel state_dict names;
+ * the embedder under "embed.", the FiLM adapter under "film.", precomputed
+ * "layers.<i>.self_attn.relative_keys" [13*hidden] f32 and
+ * "layers.<i>.self_attn.query_scale" [head_dim] f32).  GEMM weights are LB_BF16,
+ * or LB_I8 with a companion "<name>:scale" LB_F16 [rows] tensor.  Synchronous. */
+int lb_set_tensor(lb_ctx* ctx, const char* name, const void* host_data, int dtype, int64_t numel);
+/* Checks that every required parameter was uploaded.  Must precede stepping. */
+int lb_finalize_weights(lb_ctx* ctx);
+/* Number of parameter names the context expects, and the i-th name. */
+int lb_tensor_count(lb_ctx* ctx);
+const char* lb_tensor_name(lb_ctx* ctx, int index);
+
+/* Packs one step: maps rows to persistent slots on the GPU with the reference
+ * slot policy (streaming_conformer.py:571-615: existing identity -> its slot,
+ * "continue" iff the cursor equals the expected one; same session with a new
+ * generation/epoch -> its slot, "identity_reset"; new session -> lowest free
+ * slot in row order) and builds the row -> slot / reset / mask tables.
+ * handles: int32 [n] session handles in [0, max_handles); keys: int64 [n]
+ * identity (generation, epoch) tokens; frames / seqs: int64 [n] cursors;
+ * masks: uint8 [n] bit r = mel row r valid (NULL = all valid).  Device
+ * pointers.  Errors that only the device can see (exhausted bank, duplicate
+ * handle) set lb_get_status bits and leave session state untouched. */
+int lb_pack_async(lb_ctx* ctx, int n_rows, const int32_t* handles, const int64_t* keys,
+                  const int64_t* frames, const int64_t* seqs, const uint8_t* masks,
+                  void* stream);
+
+/* Runs the packed step: (PCM -> log-mel ->) Conformer -> raw / soft tokens
+ * (-> FiLM).  input: LB_INPUT_PCM float32 [n][1280] or LB_INPUT_MEL float32
+ * [n][8][128]; query: bf16 [n][2][film_query_dim] or NULL (no FiLM output);
+ * out_raw bf16 [n][2][output_dims], out_soft bf16 [n][2][text_hidden],
+ * out_film bf16 [n][2][film_query_dim] (any output may be NULL).  Writes only
+ * staged session state; canonical state advances on lb_commit_async. */
+int lb_step_async(lb_ctx* ctx, int input_kind, const void* input, const void* query,
+                  void* out_raw, void* out_soft, void* out_film, void* stream);
+
+/* Same step with HOST buffers: copies inputs in, runs pack + step, copies the
+ * outputs back and synchronises the stream before returning (end-to-end
+ * form of one serving tick).  Row arrays as in lb_pack_async, host memory. */
+int lb_step_host(lb_ctx* ctx, int n_rows, const int32_t* handles, const int64_t* keys,
+                 const int64_t* frames, const int64_t* seqs, const uint8_t* masks,
+                 int input_kind, const void* input, const void* query, void* out_raw,
+                 void* out_soft, void* out_film, int commit, void* stream);
+
+/* Optional diagnostics for the next lb_step_async (forces eager launches):
+ * subsampled float32 [n][2][hidden], layers float32 [layers][n][2][hidden]. */
+int lb_set_debug_outputs(lb_ctx* ctx, float* subsampled, float* layers);
+
+/* Commits the packed+stepped rows: checks that no cursor changed since pack
+ * (all-or-nothing, streaming_conformer.py:904-958), then installs the staged
+ * ring heads and cursors.  A stale cursor sets LB_DEV_STALE_COMMIT. */
+int lb_commit_async(lb_ctx* ctx, void* stream);
+/* Drops the packed step without touching session state (streaming_conformer.py:986-990). */
+int lb_abort(lb_ctx* ctx);
+/* Restores the state before the last commit (streaming_conformer.py:960-967).
+ * Valid only until the next lb_pack_async. */
+int lb_rollback_async(lb_ctx* ctx, void* stream);
+/* Releases one session handle (its slot becomes free, state logically zero).
+ * StreamingConformerAudioTower.reset (streaming_conformer.py:418-434). */
+int lb_reset_handle_async(lb_ctx* ctx, int32_t handle, void* stream);
+/* Releases one slot (StreamingConformerAudioTower.reset_session, :436-451). */
+int lb_reset_slot_async(lb_ctx* ctx, int32_t slot, void* stream);
+
+/* Synchronous reads (they synchronise the given stream). */
+int lb_get_status(lb_ctx* ctx, int32_t* status_out, void* stream);
+int lb_clear_status(lb_ctx* ctx, void* stream);
+/* Last packed rows: slot ids and reasons (lb_row_reason). */
+int lb_read_rows(lb_ctx* ctx, int32_t* slots_host, int32_t* reasons_host, int n, void* stream);
+/* Directory dump: per handle slot (-1 = none), key, expected frame / seq. */
+int lb_read_handles(lb_ctx* ctx, int32_t* slot_host, int64_t* key_host, int64_t* exp_frame_host,
+                    int64_t* exp_seq_host, void* stream);
+/* Test hook: overwrite one handle's expected cursor (cursor-tamper case). */
+int lb_debug_set_expected(lb_ctx* ctx, int32_t handle, int64_t frame, int64_t seq, void* stream);
+
+/* ----------------------------------------------------------------------
+ * Per-kernel entry points (one kernel each, caller-owned device buffers).
+ * ---------------------------------------------------------------------- */
+
+/* D[t,o] = sum_k X[t,k] W[o,k] (+bias[o]) on tcgen05 tensor cores.
+ * Replaces Gemma4ClippableLinear.forward / the reference Triton clipped
+ * linear (duplex_kernel/streaming_conformer_kernels.py:27-76, 110-168).
+ * x: bf16 [m, x_ld] (K-contiguous, x_ld % 8 == 0); w: bf16 [out_features, k]
+ * or int8 with w_scale fp16 [out_features]; out_mode 0 = bf16, 1 = fp32,
+ * 2 = fp32 atomic accumulate (caller zeroes out; required when splits > 1);
+ * act 1 = SiLU of the bf16-rounded product (bf16 output only).
+ * out_features % 128 == 0, k % 64 == 0. */
+int lb_op_gemm(const void* x, int x_ld, int m, const void* w, int w_int8, const void* w_scale,
+               const float* bias, int out_features, int k, void* out, int ld_out, int out_mode,
+               int act, int splits, int* status_dev, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LISTENER_B200_H_ */
