@@ -86,6 +86,9 @@ SIGNATURES: dict[str, tuple] = {
     "lb_read_rows": (I, [P, P, P, I, P]),
     "lb_read_handles": (I, [P, P, P, P, P, P]),
     "lb_debug_set_expected": (I, [P, I, I64, I64, P]),
+    "lb_debug_set_stop": (I, [P, I, I]),
+    "lb_step_kernel_count": (I, [P]),
+    "lb_debug_read_buffer": (I, [P, ctypes.c_char_p, P, ctypes.c_size_t, P]),
     "lb_op_gemm": (I, [P, I, I, P, I, P, P, I, I, P, I, I, I, I, P, P]),
 }
 

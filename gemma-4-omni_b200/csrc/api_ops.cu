@@ -8,6 +8,24 @@
 
 using namespace lb;
 
+namespace lb {
+cudaError_t gemm_init_attributes();
+}
+
+namespace {
+// The GEMM kernels need their shared-memory limit raised once per device.
+cudaError_t ensure_gemm_attributes() {
+  static unsigned long long done = 0;  // bit per device ordinal
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 64 && (done >> dev) & 1ull) return cudaSuccess;
+  e = gemm_init_attributes();
+  if (e == cudaSuccess && dev < 64) done |= 1ull << dev;
+  return e;
+}
+}  // namespace
+
 extern "C" {
 
 int lb_op_gemm(const void* x, int x_ld, int m, const void* w, int w_int8, const void* w_scale,
@@ -17,6 +35,7 @@ int lb_op_gemm(const void* x, int x_ld, int m, const void* w, int w_int8, const 
   if (w_int8 && !w_scale) return LB_ERR_INVALID_ARGUMENT;
   if (out_mode < 0 || out_mode > 2 || act < 0 || act > 1) return LB_ERR_INVALID_ARGUMENT;
   if (splits > 1 && out_mode != 2) return LB_ERR_INVALID_ARGUMENT;
+  if (ensure_gemm_attributes() != cudaSuccess) return LB_ERR_CUDA;
   GemmPlan plan;
   int rc = gemm_prepare(&plan, w, w_int8 != 0, out_features, k, x, x_ld, m);
   if (rc) return rc == -3 ? LB_ERR_INVALID_ARGUMENT : LB_ERR_CUDA;

@@ -27,7 +27,9 @@ struct lb_ctx {
     lb::GemmOp in_proj, out_proj, embed, qdown, rdown, film, fout;
     std::vector<LayerOps> layers;
     cudaGraphExec_t graph[4] = {nullptr, nullptr, nullptr, nullptr};
+    int graph_kernels[4] = {0, 0, 0, 0};
   };
+  int last_graph_kernels = 0;
   std::vector<Plans> plans;
   // pinned staging for lb_step_host
   void* pinned = nullptr;
@@ -128,6 +130,7 @@ float* reg_f32(lb_ctx* x, Arena& a, const std::string& name, int64_t numel, bool
 void reg_clip(lb_ctx* x, const std::string& prefix, float* dst4) {
   static const char* kNames[4] = {"input_min", "input_max", "output_min", "output_max"};
   for (int i = 0; i < 4; ++i) {
+    dst4[i] = (i % 2 == 0) ? -INFINITY : INFINITY;  // unclipped unless uploaded
     TensorSlot t;
     t.dst = nullptr;
     t.dtype = LB_F32;
@@ -468,6 +471,12 @@ int build_plans(lb_ctx* x, int bi) {
   return 0;
 }
 
+// Diagnostics only (eager runs): return after stage `k` of layer `i`.
+#define LB_STOP(i, k)                                                        \
+  do {                                                                       \
+    if (c.dbg_stop_layer == (i) && c.dbg_stop_stage == (k)) return cudaSuccess; \
+  } while (0)
+
 #define LB_TRY(expr)                         \
   do {                                       \
     cudaError_t _e = (expr);                 \
@@ -498,7 +507,9 @@ cudaError_t run_step(lb_ctx* x, int bi, int input_kind, bool film, cudaStream_t 
     lb_ctx::LayerOps& o = P.layers[i];
     // FFN1
     LB_TRY(run_op(c, o.ffn1[0], tc, c.xf, s));
+    LB_STOP(i, 0);
     LB_TRY(run_op(c, o.ffn1[1], tc, nullptr, s));
+    LB_STOP(i, 1);
     {
       RowFusedArgs r;
       r.y = c.y;
@@ -510,10 +521,14 @@ cudaError_t run_step(lb_ctx* x, int bi, int input_kind, bool film, cudaStream_t 
       r.xa = c.xa;
       LB_TRY(launch_row_fused(c, tc, r, s));
     }
+    LB_STOP(i, 2);
     // attention
     LB_TRY(run_op(c, o.qkv, tc, c.qkv, s));
+    LB_STOP(i, 3);
     LB_TRY(launch_attention(c, i, rc, s));
+    LB_STOP(i, 4);
     LB_TRY(run_op(c, o.post, tc, nullptr, s));
+    LB_STOP(i, 5);
     {
       RowFusedArgs r;
       r.y = c.y;
@@ -525,10 +540,14 @@ cudaError_t run_step(lb_ctx* x, int bi, int input_kind, bool film, cudaStream_t 
       r.xa = c.xa;
       LB_TRY(launch_row_fused(c, tc, r, s));
     }
+    LB_STOP(i, 6);
     // light conv
     LB_TRY(run_op(c, o.lstart, tc, c.gl, s));
+    LB_STOP(i, 7);
     LB_TRY(launch_lconv(c, i, rc, s));
+    LB_STOP(i, 8);
     LB_TRY(run_op(c, o.lend, tc, nullptr, s));
+    LB_STOP(i, 9);
     {
       RowFusedArgs r;
       r.y = c.y;
@@ -538,9 +557,12 @@ cudaError_t run_step(lb_ctx* x, int bi, int input_kind, bool film, cudaStream_t 
       r.xa = c.xa;
       LB_TRY(launch_row_fused(c, tc, r, s));
     }
+    LB_STOP(i, 10);
     // FFN2 + norm_out (+ next layer's FFN1 pre-norm, or plain bf16 for output_proj)
     LB_TRY(run_op(c, o.ffn2[0], tc, c.xf, s));
+    LB_STOP(i, 11);
     LB_TRY(run_op(c, o.ffn2[1], tc, nullptr, s));
+    LB_STOP(i, 12);
     {
       RowFusedArgs r;
       r.y = c.y;
@@ -819,7 +841,7 @@ int lb_step_async(lb_ctx* x, int kind, const void* input, const void* query, voi
   if (e == cudaSuccess && film)
     e = cudaMemcpyAsync(c.in_query, query, 2ull * n * 2 * c.cfg.film_query_dim, cudaMemcpyDefault, s);
   if (e != cudaSuccess) return LB_ERR_CUDA;
-  const bool eager = c.dbg_sub || c.dbg_layers;
+  const bool eager = c.dbg_sub || c.dbg_layers || c.dbg_stop_layer >= 0;
   lb_ctx::Plans& P = x->plans[bi];
   const int variant = kind * 2 + (film ? 1 : 0);
   if (eager) {
@@ -835,10 +857,21 @@ int lb_step_async(lb_ctx* x, int kind, const void* input, const void* query, voi
         if (graph) cudaGraphDestroy(graph);
         return LB_ERR_CUDA;
       }
+      size_t num_nodes = 0;
+      cudaGraphGetNodes(graph, nullptr, &num_nodes);
+      std::vector<cudaGraphNode_t> nodes(num_nodes);
+      cudaGraphGetNodes(graph, nodes.data(), &num_nodes);
+      int kernels = 0;
+      for (auto nd : nodes) {
+        cudaGraphNodeType t;
+        if (cudaGraphNodeGetType(nd, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) ++kernels;
+      }
+      P.graph_kernels[variant] = kernels;
       e = cudaGraphInstantiate(&P.graph[variant], graph, 0);
       cudaGraphDestroy(graph);
       if (e != cudaSuccess) return LB_ERR_CUDA;
     }
+    x->last_graph_kernels = P.graph_kernels[variant];
     e = cudaGraphLaunch(P.graph[variant], s);
   }
   if (e != cudaSuccess) return LB_ERR_CUDA;
@@ -952,6 +985,32 @@ int lb_debug_set_expected(lb_ctx* x, int32_t handle, int64_t frame, int64_t seq,
   long long f = frame, q = seq;
   cudaError_t e = cudaMemcpyAsync(c.handle_exp_frame + handle, &f, 8, cudaMemcpyHostToDevice, s);
   if (e == cudaSuccess) e = cudaMemcpyAsync(c.handle_exp_seq + handle, &q, 8, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  return err_of(e);
+}
+
+int lb_step_kernel_count(lb_ctx* x) { return x ? x->last_graph_kernels : 0; }
+
+int lb_debug_set_stop(lb_ctx* x, int layer, int stage) {
+  if (!x) return LB_ERR_INVALID_ARGUMENT;
+  x->c.dbg_stop_layer = layer;
+  x->c.dbg_stop_stage = stage;
+  return LB_OK;
+}
+
+int lb_debug_read_buffer(lb_ctx* x, const char* name, void* dst, size_t bytes, void* stream) {
+  if (!x || !name || !dst) return LB_ERR_INVALID_ARGUMENT;
+  Ctx& c = x->c;
+  const std::string n(name);
+  const void* src = n == "h" ? static_cast<const void*>(c.h) : n == "y" ? static_cast<const void*>(c.y)
+                  : n == "xa" ? static_cast<const void*>(c.xa) : n == "xf" ? static_cast<const void*>(c.xf)
+                  : n == "qkv" ? static_cast<const void*>(c.qkv) : n == "att" ? static_cast<const void*>(c.att)
+                  : n == "gl" ? static_cast<const void*>(c.gl) : n == "mel" ? static_cast<const void*>(c.in_mel)
+                  : n == "sub_in" ? static_cast<const void*>(c.sub_in) : nullptr;
+  if (!src) return LB_ERR_INVALID_ARGUMENT;
+  cudaSetDevice(c.device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, s);
   if (e == cudaSuccess) e = cudaStreamSynchronize(s);
   return err_of(e);
 }

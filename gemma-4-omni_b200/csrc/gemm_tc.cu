@@ -124,7 +124,7 @@ __global__ void __launch_bounds__(GemmCfg<TN, WINT8>::kThreads, 1)
     if (lane == 0) {
       const uint64_t pol_w = l2_policy_evict_first();
       const uint64_t pol_x = l2_policy_evict_last();
-      const uint32_t tx = (WINT8 ? kRawBytes : kABytes) + Cfg::kBBytes;
+      const uint32_t tx = (WINT8 ? kRawBytes : kABytes) + p.b_tx_bytes;
       for (int i = 0; i < nkb; ++i) {
         const int s = i % S;
         const uint32_t ph = (i / S) & 1;
@@ -318,15 +318,21 @@ int gemm_prepare(GemmPlan* plan, const void* w, bool w_int8, int O, int K, const
                             kBlockO, true);
   }
   if (rc) return rc;
-  // Rows past m_cap are outside the tensor map: TMA zero-fills them, so the
-  // activation buffer needs exactly m_cap rows.
+  // The activation map covers exactly m_cap rows (TMA zero-fills rows past it).
+  // A box may not exceed the tensor extent, so with fewer rows than the token
+  // tile the box shrinks to m_cap rows; the tile's remaining shared-memory rows
+  // then hold stale data that only reaches output columns t >= m_cap, which the
+  // epilogue never stores.
+  plan->x_box_rows = m_cap < plan->tn ? m_cap : plan->tn;
   return make_tensor_map_2d(&plan->tm_x, x, 2, K, static_cast<uint64_t>(m_cap),
-                            static_cast<uint64_t>(x_ld) * 2, kBlockK, plan->tn, true);
+                            static_cast<uint64_t>(x_ld) * 2, kBlockK,
+                            static_cast<uint32_t>(plan->x_box_rows), true);
 }
 
 cudaError_t gemm_launch(const GemmPlan& plan, GemmParams p, int splits, cudaStream_t stream) {
   p.O = plan.O;
   p.K = plan.K;
+  p.b_tx_bytes = static_cast<uint32_t>(plan.x_box_rows) * kBlockK * 2;
   const int total_kb = plan.K / kBlockK;
   if (splits < 1) splits = 1;
   if (splits > total_kb) splits = total_kb;

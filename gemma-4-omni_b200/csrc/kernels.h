@@ -28,12 +28,14 @@ struct GemmParams {
   float out_lo = -INFINITY, out_hi = INFINITY;    // linear output clamp (before act)
   float post_lo = -INFINITY, post_hi = INFINITY;  // next linear's input clamp (after act)
   int* status = nullptr;
+  uint32_t b_tx_bytes = 0;  // bytes one activation-tile TMA load delivers (set by gemm_launch)
 };
 
 struct GemmPlan {
   CUtensorMap tm_w;
   CUtensorMap tm_x;
   int O = 0, K = 0, m_cap = 0, tn = 0;
+  int x_box_rows = 0;  // rows per activation TMA box: min(tn, m_cap)
   bool w_int8 = false;
 };
 

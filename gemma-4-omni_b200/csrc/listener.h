@@ -192,6 +192,8 @@ struct Ctx {
   // optional per-layer debug outputs (null in serving)
   float* dbg_sub = nullptr;
   float* dbg_layers = nullptr;
+  int dbg_stop_layer = -1;  // eager diagnostics: stop after (layer, stage)
+  int dbg_stop_stage = -1;
 
   // frontend tables: periodic Hann window [320], DFT twiddles [512] x2,
   // mel filterbank [257][128] and its non-zero row range per mel bin

@@ -160,9 +160,11 @@ class ArrivalProcess:
             self.pos = np.zeros(num_sessions, dtype=np.int64)
         else:
             self.start = np.zeros(num_sessions, dtype=np.int64)
-            self.length = self.rng.geometric(p, size=num_sessions)
-            # lanes start mid-session so cache positions differ from step 0
-            self.pos = (self.rng.random(num_sessions) * self.length).astype(np.int64)
+            # start in the stationary state of back-to-back geometric sessions:
+            # both the age and the remaining life of a live session are geometric,
+            # so cache positions differ from step 0 and ~num/mean_len join per step
+            self.pos = self.rng.geometric(p, size=num_sessions).astype(np.int64) - 1
+            self.length = self.pos + self.rng.geometric(p, size=num_sessions)
             self.session_id = np.arange(num_sessions, dtype=np.int64)
             self._next_id = num_sessions
         self.step_index = 0

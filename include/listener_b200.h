@@ -164,6 +164,9 @@ int lb_reset_handle_async(lb_ctx* ctx, int32_t handle, void* stream);
 /* Releases one slot (StreamingConformerAudioTower.reset_session, :436-451). */
 int lb_reset_slot_async(lb_ctx* ctx, int32_t slot, void* stream);
 
+/* Kernels launched by the CUDA graph of the last lb_step_async (0 if eager). */
+int lb_step_kernel_count(lb_ctx* ctx);
+
 /* Synchronous reads (they synchronise the given stream). */
 int lb_get_status(lb_ctx* ctx, int32_t* status_out, void* stream);
 int lb_clear_status(lb_ctx* ctx, void* stream);
@@ -174,6 +177,12 @@ int lb_read_handles(lb_ctx* ctx, int32_t* slot_host, int64_t* key_host, int64_t*
                     int64_t* exp_seq_host, void* stream);
 /* Test hook: overwrite one handle's expected cursor (cursor-tamper case). */
 int lb_debug_set_expected(lb_ctx* ctx, int32_t handle, int64_t frame, int64_t seq, void* stream);
+/* Diagnostics: make the next lb_step_async run eagerly and stop after stage
+ * `stage` (0..12) of layer `layer` (-1 disables); lb_debug_read_buffer copies
+ * an internal activation ("h", "y", "xa", "xf", "qkv", "att", "gl", "mel",
+ * "sub_in") to host memory (synchronous). */
+int lb_debug_set_stop(lb_ctx* ctx, int layer, int stage);
+int lb_debug_read_buffer(lb_ctx* ctx, const char* name, void* host_dst, size_t bytes, void* stream);
 
 /* ----------------------------------------------------------------------
  * Per-kernel entry points (one kernel each, caller-owned device buffers).

@@ -1,0 +1,231 @@
+"""Listener step on the GPU vs the reference goldens and the CPU oracle.
+
+Tolerance (bf16 weights/activations vs the fp32 reference): per-frame cosine
+>= 0.999 and max|a-b|/max|b| <= 2e-2 (tests/helpers.py).  Packing (slot ids,
+reasons) is compared bit-exactly.
+"""
+from __future__ import annotations
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import (HandleBook, assert_parity, film_weights_from_engine, golden_rows, mask_bits,
+                     oracle_from_engine)
+from oracle import conformer_ref, film_ref, mel_ref
+
+pytestmark = pytest.mark.gpu
+GOLD = Path(__file__).resolve().parent / "golden"
+REASON_CODES = {"continue": 0, "reset": 1, "gap_or_cursor_mismatch": 2, "identity_reset": 3}
+
+
+def make_engine(cfg, fmt=0, sessions=8, rows=None, tower_seed=11, film_seed=12, film_scale=1.0, handles=None):
+    from gemma4_omni_b200 import runtime, synthetic
+
+    eng = runtime.ListenerEngine(cfg, max_sessions=sessions, max_rows=rows, max_handles=handles,
+                                 weight_format=fmt)
+    fw = synthetic.synthetic_film_weights(cfg, film_seed)
+    fw["output.weight"] = fw["output.weight"] * film_scale
+    eng.load_weights(synthetic.synthetic_tower_weights(cfg, tower_seed), fw)
+    return eng
+
+
+def replay_golden(eng, g, debug=True):
+    rows, reasons = golden_rows(g)
+    book = HandleBook()
+    off = 0
+    outs = {"raw": [], "soft": [], "sub": [], "layers": []}
+    for tick_rows, tick_reasons in zip(rows, reasons):
+        n = len(tick_rows)
+        h, k, f, q = book.arrays(tick_rows)
+        eng.pack(h, k, f, q, mask_bits(g["mask"][off:off + n]))
+        mel = torch.from_numpy(g["mel"][off:off + n]).cuda()
+        out = eng.step(mel, kind=1, debug=debug)
+        slots, rs = eng.read_rows(n)
+        assert list(slots) == [int(s) for s in g["slots"][off:off + n]]
+        assert list(rs) == [REASON_CODES[r] for r in tick_reasons]
+        eng.commit()
+        outs["raw"].append(out["raw"].float().cpu())
+        outs["soft"].append(out["soft"].float().cpu())
+        if debug:
+            outs["sub"].append(out["subsampled"].cpu())
+            outs["layers"].append(out["layers"].cpu())
+        off += n
+    assert eng.status() == 0
+    return {k: torch.cat(v, dim=1 if k == "layers" else 0) for k, v in outs.items() if v}
+
+
+@pytest.mark.parametrize("fmt", [0, 1])
+def test_small_tower_replays_reference_trace(pkg, fmt):
+    """Reorder, reset, cursor gap, epoch change and input masks (reference trace)."""
+    from gemma4_omni_b200.config import SMALL
+
+    g = np.load(GOLD / "tower_small.npz")
+    eng = make_engine(SMALL, fmt, sessions=6, tower_seed=int(g["seed_w"]))
+    out = replay_golden(eng, g)
+    # the golden is the fp32 reference; int8 adds quantisation error on top of bf16
+    cos_min = 0.999 if fmt == 0 else 0.995
+    assert_parity(out["sub"], torch.from_numpy(g["sub"]), "subsampled", cos_min)
+    assert_parity(out["layers"], torch.from_numpy(g["layers"]), "layers", cos_min, 4e-2 if fmt else 2e-2)
+    assert_parity(out["raw"], torch.from_numpy(g["raw"]), "raw", cos_min, 4e-2 if fmt else 2e-2)
+    assert_parity(out["soft"], torch.from_numpy(g["soft"]), "soft", cos_min, 4e-2 if fmt else 2e-2)
+    eng.close()
+
+
+def test_full_tower_matches_reference_golden(pkg):
+    from gemma4_omni_b200.config import FULL
+
+    g = np.load(GOLD / "tower_full.npz")
+    eng = make_engine(FULL, 0, sessions=4, tower_seed=int(g["seed_w"]))
+    out = replay_golden(eng, g)
+    assert_parity(out["sub"], torch.from_numpy(g["sub"]), "subsampled")
+    assert_parity(out["raw"], torch.from_numpy(g["raw"]), "raw")
+    assert_parity(out["soft"], torch.from_numpy(g["soft"]), "soft")
+    eng.close()
+
+
+def test_mel_kernel_matches_reference_extractor(pkg):
+    """Fused STFT/mel/log on the GPU vs the reference _extract_single_frame goldens."""
+    from gemma4_omni_b200 import _lib
+    from gemma4_omni_b200.config import SMALL
+
+    g = np.load(GOLD / "mel.npz")
+    eng = make_engine(SMALL, 0, sessions=4)
+    pcm = g["pcm"].reshape(3, 6, 1280)
+    got = []
+    for f in range(6):
+        h = torch.arange(3, dtype=torch.int32, device="cuda")
+        z = torch.zeros(3, dtype=torch.int64, device="cuda")
+        fr = torch.full((3,), f, dtype=torch.int64, device="cuda")
+        eng.pack(h, z, fr, fr.clone())
+        eng.step(torch.from_numpy(np.ascontiguousarray(pcm[:, f])).cuda(), kind=_lib.LB_INPUT_PCM)
+        buf = np.zeros(3 * 8 * 128, np.float32)
+        eng.lib.lb_debug_read_buffer(eng._ctx, b"mel", buf.ctypes.data, buf.nbytes, eng._stream)
+        got.append(buf.reshape(3, 8, 128))
+        eng.commit()
+    got = np.stack(got, axis=1).reshape(18, 8, 128)
+    ref = g["mel"]
+    # fp32 DFT vs the reference's float64 rfft; log compresses absolute error
+    np.testing.assert_allclose(got, ref, rtol=0, atol=2e-4)
+    assert np.abs(got - ref).mean() < 2e-5
+    eng.close()
+
+
+@pytest.mark.parametrize("fmt,steps,n", [(0, 500, 2), (1, 200, 2)])
+def test_full_config_carried_parity_over_many_steps(pkg, fmt, steps, n):
+    """PCM -> soft tokens, state carried across `steps` ticks, vs the CPU oracle."""
+    from gemma4_omni_b200 import _lib, synthetic
+    from gemma4_omni_b200.config import FULL
+
+    torch.set_num_threads(max(1, torch.get_num_threads()))
+    eng = make_engine(FULL, fmt, sessions=4)
+    model = oracle_from_engine(eng)
+    state = conformer_ref.zero_state(model.cfg, n)
+    pcm_all = np.stack([synthetic.session_audio(21, s, steps, total_frames=steps) for s in range(n)], axis=1)
+    tails = [None] * n
+    worst_cos, worst_rel = 1.0, 0.0
+    h = torch.arange(n, dtype=torch.int32, device="cuda")
+    z = torch.zeros(n, dtype=torch.int64, device="cuda")
+    for t in range(steps):
+        fr = torch.full((n,), t, dtype=torch.int64, device="cuda")
+        eng.pack(h, z, fr, fr.clone())
+        pcm = pcm_all[t]
+        out = eng.step(torch.from_numpy(np.ascontiguousarray(pcm)).cuda(), kind=_lib.LB_INPUT_PCM)
+        eng.commit()
+        mels = []
+        for i in range(n):
+            m, tails[i] = mel_ref.extract_single_frame(pcm[i], tails[i])
+            mels.append(m)
+        reset = torch.full((n,), t == 0)
+        _, soft, _, _, state = model.step(torch.from_numpy(np.stack(mels)), torch.ones(n, 8, dtype=torch.bool),
+                                          state, reset)
+        c, r = assert_parity(out["soft"], soft, f"soft step {t}", 0.999 if fmt == 0 else 0.998,
+                             2e-2 if fmt == 0 else 3e-2)
+        worst_cos, worst_rel = min(worst_cos, c), max(worst_rel, r)
+    assert eng.status() == 0
+    print(f"fmt={fmt} steps={steps}: worst cosine {worst_cos:.6f}, worst rel {worst_rel:.3e}")
+    eng.close()
+
+
+def test_ragged_continuous_batching_matches_oracle(pkg):
+    """Sessions join/leave every step, rows arrive in shuffled order (BASELINE config 2 style)."""
+    from gemma4_omni_b200 import _lib, synthetic
+    from gemma4_omni_b200.config import SMALL
+
+    rng = np.random.default_rng(5)
+    eng = make_engine(SMALL, 0, sessions=24, rows=24, film_scale=300.0, handles=64)
+    model = oracle_from_engine(eng)
+    fw = film_weights_from_engine(eng)
+    arrivals = synthetic.ArrivalProcess(40, seed=3, mean_len=12, start_max=20, mode="pool")
+    states: dict[int, dict] = {}
+    zero = {k: v[0] for k, v in conformer_ref.zero_state(model.cfg, 1).items()}
+    tails: dict[int, np.ndarray | None] = {}
+    for t in range(40):
+        lanes, sids, frames, _ = arrivals.step()
+        # sessions that ended last step release their slot
+        for sid in list(states):
+            if sid not in set(int(s) for s in sids):
+                eng.reset_handle(sid)
+                states.pop(sid)
+        if len(sids) == 0:
+            continue
+        order = rng.permutation(len(sids))
+        sids, frames = sids[order], frames[order]
+        n = len(sids)
+        h = torch.from_numpy(sids.astype(np.int32)).cuda()
+        z = torch.zeros(n, dtype=torch.int64, device="cuda")
+        fr = torch.from_numpy(frames.astype(np.int64)).cuda()
+        eng.pack(h, z, fr, fr.clone())
+        pcm = np.stack([synthetic.session_audio(9, int(s), 1, first_frame=int(f), total_frames=64)[0]
+                        for s, f in zip(sids, frames)])
+        query = torch.randn(n, 2, SMALL.film_query_dim, generator=torch.Generator().manual_seed(t)).to(torch.bfloat16)
+        out = eng.step(torch.from_numpy(pcm).cuda(), kind=_lib.LB_INPUT_PCM, query=query.cuda())
+        eng.commit()
+        mels = []
+        for i, s in enumerate(sids):
+            m, tails[int(s)] = mel_ref.extract_single_frame(pcm[i], tails.get(int(s)) if frames[i] > 0 else None)
+            mels.append(m)
+        st = {k: torch.stack([states.get(int(s), zero)[k] for s in sids]) for k in zero}
+        reset = torch.tensor([int(s) not in states for s in sids])
+        raw, soft, _, _, nxt = model.step(torch.from_numpy(np.stack(mels)), torch.ones(n, 8, dtype=torch.bool),
+                                          st, reset)
+        for i, s in enumerate(sids):
+            states[int(s)] = {k: v[i] for k, v in nxt.items()}
+        assert_parity(out["raw"], raw, f"raw step {t}")
+        assert_parity(out["soft"], soft, f"soft step {t}")
+        ref_film = film_ref.film_forward(fw, out["soft"].float().cpu(), query.float())
+        assert_parity(out["film"], ref_film, f"film step {t}", 0.9999, 1e-2)
+    assert eng.status() == 0
+    eng.close()
+
+
+def test_step_host_matches_device_path(pkg):
+    """lb_step_host (host buffers, H2D/D2H inside the call) equals lb_step_async outputs."""
+    from gemma4_omni_b200 import _lib, synthetic
+    from gemma4_omni_b200.config import SMALL
+
+    n = 5
+    a = make_engine(SMALL, 1, sessions=8)
+    b = make_engine(SMALL, 1, sessions=8)
+    handles = np.arange(n, dtype=np.int32)
+    keys = np.zeros(n, np.int64)
+    for t in range(3):
+        frames = np.full(n, t, np.int64)
+        pcm = np.stack([synthetic.session_audio(1, s, 1, first_frame=t, total_frames=3)[0] for s in range(n)])
+        query = torch.randn(n, 2, SMALL.film_query_dim, generator=torch.Generator().manual_seed(t)).to(torch.bfloat16)
+        a.pack(torch.from_numpy(handles).cuda(), torch.from_numpy(keys).cuda(), torch.from_numpy(frames).cuda(),
+               torch.from_numpy(frames).cuda())
+        oa = a.step(torch.from_numpy(pcm).cuda(), kind=_lib.LB_INPUT_PCM, query=query.cuda())
+        a.commit()
+        soft = np.zeros((n, 2, SMALL.text_hidden), np.uint16)
+        film = np.zeros((n, 2, SMALL.film_query_dim), np.uint16)
+        qb = query.view(torch.int16).numpy().view(np.uint16)
+        b.step_host(handles, keys, frames, frames.copy(), pcm, query=qb, out_soft=soft, out_film=film)
+        # same kernels; only the fp32 split-K reduction order may differ between runs
+        as_f32 = lambda u: torch.from_numpy((u.astype(np.uint32) << 16).view(np.float32))
+        assert_parity(oa["soft"], as_f32(soft), "step_host soft", 0.99999, 1e-2)
+        assert_parity(oa["film"], as_f32(film), "step_host film", 0.99999, 1e-2)
+    a.close()
+    b.close()
