@@ -37,7 +37,7 @@ int lb_op_gemm(const void* x, int x_ld, int m, const void* w, int w_int8, const 
   if (splits > 1 && out_mode != 2) return LB_ERR_INVALID_ARGUMENT;
   if (ensure_gemm_attributes() != cudaSuccess) return LB_ERR_CUDA;
   GemmPlan plan;
-  int rc = gemm_prepare(&plan, w, w_int8 != 0, out_features, k, x, x_ld, m);
+  int rc = gemm_prepare(&plan, w, w_int8 != 0, out_features, k, x, x_ld, m, out, ld_out, out_mode);
   if (rc) return rc == -3 ? LB_ERR_INVALID_ARGUMENT : LB_ERR_CUDA;
   GemmParams p;
   p.m_static = m;

@@ -384,8 +384,6 @@ int make_op(Ctx& c, GemmOp& op, void* w, const __half* scale, int O, int K, cons
             const float* bias, void* out, int out_kind, int act, const float* clip4,
             float post_lo = -INFINITY, float post_hi = INFINITY, __nv_bfloat16* final_bf16 = nullptr) {
   // out_kind: 0 = bf16 (final), 1 = fp32
-  int rc = gemm_prepare(&op.plan, w, c.weight_int8 != 0, O, K, x, K, tok_cap);
-  if (rc) return rc;
   GemmParams& p = op.params;
   p = GemmParams();
   p.m_dev = c.dev_counts + 1;
@@ -401,7 +399,7 @@ int make_op(Ctx& c, GemmOp& op, void* w, const __half* scale, int O, int K, cons
   p.post_lo = post_lo;
   p.post_hi = post_hi;
   const bool finite_out = std::isfinite(p.out_lo) || std::isfinite(p.out_hi);
-  op.splits = finite_out && out_kind == 1 ? 1 : gemm_pick_splits(op.plan, c.num_sms);
+  op.splits = finite_out && out_kind == 1 ? 1 : gemm_pick_splits(O, K, tok_cap, c.num_sms);
   if (op.splits > 1) {
     p.out_mode = 2;
     p.out = out_kind == 0 ? static_cast<void*>(c.wide_acc) : out;
@@ -410,7 +408,7 @@ int make_op(Ctx& c, GemmOp& op, void* w, const __half* scale, int O, int K, cons
     p.out = out;
   }
   (void)final_bf16;
-  return 0;
+  return gemm_prepare(&op.plan, w, c.weight_int8 != 0, O, K, x, K, tok_cap, p.out, O, p.out_mode);
 }
 
 cudaError_t run_op(Ctx& c, const GemmOp& op, int tok_cap, __nv_bfloat16* final_bf16, cudaStream_t s) {

@@ -12,20 +12,24 @@
 // Design (swap-AB): the UMMA M dimension (128) runs over output features, the
 // UMMA N dimension over tokens (TN = 32..256), so a step with 2 tokens streams
 // weights through the tensor core exactly like a step with 2048 tokens, only
-// with a narrower N.  Operands are staged by TMA (128-byte swizzle, no
-// multicast) into a STAGES-deep shared-memory ring; one thread issues
-// tcgen05.mma into a TMEM accumulator of 128 lanes x TN fp32 columns; four
-// epilogue warps drain TMEM with tcgen05.ld and apply the per-channel int8
-// scale, bias, activation and output rounding.
+// with a narrower N.
 //
-// Weight-only int8: W arrives as int8 rows with one fp16 scale per output
-// channel.  Four converter warps widen each staged int8 tile to bf16 (exact:
-// every int8 value is a bf16 value) directly into the 128-byte-swizzled layout
-// UMMA reads; the scale is applied per accumulator lane in the epilogue, which
-// equals x . (q * s) up to fp32 summation order.
-//
-// Split-K: grid.z splits the K loop; splits accumulate with fp32 reductions
-// into a zeroed fp32 buffer (out_mode 2) that a finalize pass consumes.
+// Persistent, warp-specialised: one CTA per SM walks a list of work units
+// (output tile, token tile, K split), output tiles fastest so concurrently
+// running CTAs share the activation tile in L2.
+//   warp 0      TMA producer: W and X tiles into a STAGES-deep smem ring
+//               (128-byte swizzle; no multicast anywhere)
+//   warp 1      UMMA issuer: tcgen05.mma into one of two TMEM accumulators
+//               (2 x TN fp32 columns), so the epilogue of one unit overlaps the
+//               main loop of the next
+//   warps 2..5  epilogue: tcgen05.ld -> per-channel int8 scale, bias, clamps,
+//               SiLU -> [32 tokens x 128 features] smem staging -> TMA store
+//               (or TMA reduce-add for split-K partial sums)
+//   warps 6..13 int8 only: widen each staged int8 weight tile to bf16 directly
+//               in the 128-byte-swizzled layout UMMA reads (exact: every int8
+//               is a bf16); the scale is applied per accumulator lane.
+// Every wait is bounded (common.cuh); on a timeout the kernel records
+// kStatusWaitTimeout, drains its outstanding stores and frees its TMEM.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -41,33 +45,101 @@ constexpr int kBlockO = 128;
 constexpr int kBlockK = 64;
 constexpr uint32_t kABytes = kBlockO * kBlockK * 2;  // bf16 A tile, 16 KB
 constexpr uint32_t kRawBytes = kBlockO * kBlockK;    // int8 A tile, 8 KB
+constexpr int kChunk = 32;                           // tokens per epilogue chunk
+constexpr uint32_t kStagingBytes = kChunk * kBlockO * 4;  // one fp32 staging buffer, 16 KB
 
 template <int TN, bool WINT8>
 struct GemmCfg {
-  static constexpr int kStages = WINT8 ? (TN >= 256 ? 3 : 4) : (TN >= 256 ? 4 : 6);
   static constexpr uint32_t kBBytes = TN * kBlockK * 2;
   static constexpr uint32_t kStageBytes = kABytes + kBBytes + (WINT8 ? kRawBytes : 0);
-  static constexpr uint32_t kBarBytes = (4 * kStages + 2) * 8 + 16;
-  static constexpr uint32_t kSmemBytes = kStages * kStageBytes + kBarBytes + 1024;
-  static constexpr int kThreads = WINT8 ? 320 : 192;
-  static constexpr uint32_t kTmemCols = TN;  // power of two >= 32
+  // operand ring + 2 staging buffers within 224 KB (the 227 KB opt-in limit
+  // leaves room for barriers and the 1 KB alignment slack)
+  static constexpr int kStages = (224 * 1024 - 2 * kStagingBytes) / kStageBytes > 8
+                                     ? 8
+                                     : (224 * 1024 - 2 * kStagingBytes) / kStageBytes;
+  static constexpr uint32_t kBarBytes = (3 * kStages + 4) * 8 + 16;
+  static constexpr uint32_t kSmemBytes =
+      kStages * kStageBytes + 2 * kStagingBytes + kBarBytes + 1024;
+  static constexpr int kThreads = WINT8 ? 448 : 192;
+  static constexpr uint32_t kTmemCols = 2 * TN;  // double-buffered accumulator
 };
 
+// Widens 16 int8 to 16 bf16 with full-rate integer/FP ops: flipping the sign
+// bit maps v to u = v + 128 in [0, 255]; placing u in the low mantissa byte of
+// the float 2^23 (bits 0x4B0000uu) gives exactly 2^23 + u, and subtracting
+// 2^23 + 128 recovers v exactly.  |v| <= 128 is exact in bf16.
 __device__ __forceinline__ void convert_i8x16_to_bf16(const int4 raw, int4& lo, int4& hi) {
-  const int8_t* b = reinterpret_cast<const int8_t*>(&raw);
+  const uint32_t w[4] = {static_cast<uint32_t>(raw.x) ^ 0x80808080u, static_cast<uint32_t>(raw.y) ^ 0x80808080u,
+                         static_cast<uint32_t>(raw.z) ^ 0x80808080u, static_cast<uint32_t>(raw.w) ^ 0x80808080u};
   __nv_bfloat162 out[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    out[i] = __floats2bfloat162_rn(static_cast<float>(b[2 * i]), static_cast<float>(b[2 * i + 1]));
+  for (int i = 0; i < 4; ++i) {
+    const float f0 = __int_as_float(__byte_perm(w[i], 0x4B000000u, 0x7540)) - 8388736.0f;
+    const float f1 = __int_as_float(__byte_perm(w[i], 0x4B000000u, 0x7541)) - 8388736.0f;
+    const float f2 = __int_as_float(__byte_perm(w[i], 0x4B000000u, 0x7542)) - 8388736.0f;
+    const float f3 = __int_as_float(__byte_perm(w[i], 0x4B000000u, 0x7543)) - 8388736.0f;
+    out[2 * i] = __floats2bfloat162_rn(f0, f1);
+    out[2 * i + 1] = __floats2bfloat162_rn(f2, f3);
   }
   lo = *reinterpret_cast<int4*>(&out[0]);
   hi = *reinterpret_cast<int4*>(&out[4]);
 }
 
+__device__ __forceinline__ void tma_load_2d_nohint(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                                   int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1)
+               : "memory");
+}
+
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const void* src, int c0,
+                                                  int c1) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read1() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+struct Unit {
+  int o0, t0, kb_begin, nkb, split;
+};
+
+__device__ __forceinline__ Unit unit_of(int u, int o_tiles, int t_tiles, int TN, int kb_per_split,
+                                        int total_kb) {
+  Unit r;
+  const int per_split = o_tiles * t_tiles;
+  r.split = u / per_split;
+  const int rem = u - r.split * per_split;
+  const int tt = rem / o_tiles;
+  r.o0 = (rem - tt * o_tiles) * kBlockO;
+  r.t0 = tt * TN;
+  r.kb_begin = r.split * kb_per_split;
+  const int kb_end = min(r.kb_begin + kb_per_split, total_kb);
+  r.nkb = kb_end - r.kb_begin;
+  return r;
+}
+
 template <int TN, bool WINT8>
 __global__ void __launch_bounds__(GemmCfg<TN, WINT8>::kThreads, 1)
     gemm_wx_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
-                   const GemmParams p) {
+                   const __grid_constant__ CUtensorMap tm_out, const GemmParams p) {
   using Cfg = GemmCfg<TN, WINT8>;
   constexpr int S = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -75,24 +147,23 @@ __global__ void __launch_bounds__(GemmCfg<TN, WINT8>::kThreads, 1)
                                              ~static_cast<uintptr_t>(1023));
 
   const int M = p.m_dev ? *p.m_dev : p.m_static;
-  const int t0 = blockIdx.y * TN;
-  if (t0 >= M) return;
-  const int o0 = blockIdx.x * kBlockO;
+  const int o_tiles = p.O / kBlockO;
+  const int t_tiles = (M + TN - 1) / TN;
   const int total_kb = p.K / kBlockK;
-  const int kb_begin = blockIdx.z * p.kb_per_split;
-  const int kb_end = min(kb_begin + p.kb_per_split, total_kb);
-  if (kb_begin >= kb_end) return;
-  const int nkb = kb_end - kb_begin;
+  const int splits = (total_kb + p.kb_per_split - 1) / p.kb_per_split;
+  const int units = o_tiles * t_tiles * splits;
 
   auto stage_a = [&](int s) { return smem + s * Cfg::kStageBytes; };
   auto stage_b = [&](int s) { return smem + s * Cfg::kStageBytes + kABytes; };
   auto stage_raw = [&](int s) { return smem + s * Cfg::kStageBytes + kABytes + Cfg::kBBytes; };
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  uint8_t* staging = smem + S * Cfg::kStageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(staging + 2 * kStagingBytes);
   uint64_t* full = bars;
   uint64_t* empty = bars + S;
   uint64_t* conv = bars + 2 * S;
-  uint64_t* tmem_full = bars + 4 * S;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4 * S + 2);
+  uint64_t* tmem_full = bars + 3 * S;       // [2]
+  uint64_t* tmem_empty = bars + 3 * S + 2;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * S + 4);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -101,14 +172,18 @@ __global__ void __launch_bounds__(GemmCfg<TN, WINT8>::kThreads, 1)
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
-      if (WINT8) mbar_init(&conv[s], 128);
+      if (WINT8) mbar_init(&conv[s], 8);
     }
-    mbar_init(tmem_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tmem_full[b], 1);
+      mbar_init(&tmem_empty[b], 4);
+    }
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tm_w);
     tma_prefetch_desc(&tm_x);
+    tma_prefetch_desc(&tm_out);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, Cfg::kTmemCols);
@@ -122,101 +197,152 @@ __global__ void __launch_bounds__(GemmCfg<TN, WINT8>::kThreads, 1)
   if (warp == 0) {
     // ---------------- TMA producer
     if (lane == 0) {
-      const uint64_t pol_w = l2_policy_evict_first();
       const uint64_t pol_x = l2_policy_evict_last();
       const uint32_t tx = (WINT8 ? kRawBytes : kABytes) + p.b_tx_bytes;
-      for (int i = 0; i < nkb; ++i) {
-        const int s = i % S;
-        const uint32_t ph = (i / S) & 1;
-        if (!mbar_wait(&empty[s], ph ^ 1, p.status)) break;
-        mbar_arrive_expect_tx(&full[s], tx);
-        const int k = (kb_begin + i) * kBlockK;
-        tma_load_2d(WINT8 ? stage_raw(s) : stage_a(s), &tm_w, &full[s], k, o0, pol_w);
-        tma_load_2d(stage_b(s), &tm_x, &full[s], k, t0, pol_x);
+      int it = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        const Unit w = unit_of(u, o_tiles, t_tiles, TN, p.kb_per_split, total_kb);
+        for (int i = 0; i < w.nkb; ++i, ++it) {
+          const int s = it % S;
+          const uint32_t ph = (it / S) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, p.status)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], tx);
+          const int k = (w.kb_begin + i) * kBlockK;
+          tma_load_2d_nohint(WINT8 ? stage_raw(s) : stage_a(s), &tm_w, &full[s], k, w.o0);
+          tma_load_2d(stage_b(s), &tm_x, &full[s], k, w.t0, pol_x);
+        }
       }
     }
   } else if (warp == 1) {
     // ---------------- UMMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc_bf16(kBlockO, TN);
+      int it = 0, local = 0;
       bool ok = true;
-      for (int i = 0; i < nkb && ok; ++i) {
-        const int s = i % S;
-        const uint32_t ph = (i / S) & 1;
-        ok = mbar_wait(&full[s], ph, p.status);
-        if (ok && WINT8) ok = mbar_wait(&conv[s], ph, p.status);
-        if (!ok) break;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++local) {
+        const Unit w = unit_of(u, o_tiles, t_tiles, TN, p.kb_per_split, total_kb);
+        const int b = local & 1;
+        const uint32_t aph = (local >> 1) & 1;
+        if (!mbar_wait(&tmem_empty[b], aph ^ 1, p.status)) break;
         tc_fence_after();
-        const uint64_t a_desc = smem_desc_k128(smem_u32(stage_a(s)));
-        const uint64_t b_desc = smem_desc_k128(smem_u32(stage_b(s)));
+        const uint32_t acc = tmem_base + static_cast<uint32_t>(b * TN);
+        for (int i = 0; i < w.nkb; ++i, ++it) {
+          const int s = it % S;
+          const uint32_t ph = (it / S) & 1;
+          ok = mbar_wait(&full[s], ph, p.status);
+          if (ok && WINT8) ok = mbar_wait(&conv[s], ph, p.status);
+          if (!ok) break;
+          tc_fence_after();
+          const uint64_t a_desc = smem_desc_k128(smem_u32(stage_a(s)));
+          const uint64_t b_desc = smem_desc_k128(smem_u32(stage_b(s)));
 #pragma unroll
-        for (int j = 0; j < kBlockK / 16; ++j) {
-          // advance 16 bf16 = 32 bytes along K inside the swizzled row
-          umma_bf16(tmem_base, a_desc + static_cast<uint64_t>(j * 2),
-                    b_desc + static_cast<uint64_t>(j * 2), idesc, (i > 0 || j > 0) ? 1u : 0u);
+          for (int j = 0; j < kBlockK / 16; ++j) {
+            // advance 16 bf16 = 32 bytes along K inside the swizzled row
+            umma_bf16(acc, a_desc + static_cast<uint64_t>(j * 2), b_desc + static_cast<uint64_t>(j * 2),
+                      idesc, (i > 0 || j > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[s]);
         }
-        umma_commit(&empty[s]);
+        if (ok) umma_commit(&tmem_full[b]);
       }
-      if (ok) umma_commit(tmem_full);
     }
   } else if (warp < 6) {
-    // ---------------- epilogue: TMEM -> registers -> global
+    // ---------------- epilogue: TMEM -> registers -> smem staging -> TMA store
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const int o = o0 + q * 32 + lane;
-    const bool ok = mbar_wait(tmem_full, 0, p.status);
-    tc_fence_after();
-    if (ok) {
+    const int et = threadIdx.x - 64;
+    const bool leader = et == 0;
+    int local = 0, chunks_issued = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
+      const Unit w = unit_of(u, o_tiles, t_tiles, TN, p.kb_per_split, total_kb);
+      const int b = local & 1;
+      const uint32_t aph = (local >> 1) & 1;
+      if (!mbar_wait(&tmem_full[b], aph, p.status)) break;
+      tc_fence_after();
+      const int o = w.o0 + q * 32 + lane;
       const float scale = WINT8 ? __half2float(p.w_scale[o]) : 1.0f;
-      const float bias = (p.bias && blockIdx.z == 0) ? p.bias[o] : 0.0f;  // once across splits
+      const float bias = (p.bias && w.split == 0) ? p.bias[o] : 0.0f;
 #pragma unroll 1
-      for (int c = 0; c < TN; c += 32) {
+      for (int c = 0; c < TN; c += kChunk) {
         float v[32];
-        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + c, v);
-        if (t0 + c >= M) continue;
+        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                               static_cast<uint32_t>(b * TN + c), v);
+        if (w.t0 + c >= M) continue;  // uniform across the epilogue warps
+        uint8_t* stg = staging + (chunks_issued & 1) * kStagingBytes;
+        if (leader && chunks_issued >= 2) bulk_wait_read1();  // this buffer's previous store has read smem
+        epi_bar();
+        if (p.out_mode == 0) {
+          __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(stg);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int t = t0 + c + j;
-          if (t < M) {
-            float y = v[j] * scale + bias;
-            const size_t idx = static_cast<size_t>(t) * p.ld_out + o;
-            if (p.out_mode == 0) {
-              y = fminf(fmaxf(y, p.out_lo), p.out_hi);
-              if (p.act == 1) y = silu_f(bf16_round(y));
-              y = fminf(fmaxf(y, p.post_lo), p.post_hi);
-              reinterpret_cast<__nv_bfloat16*>(p.out)[idx] = __float2bfloat16_rn(y);
-            } else if (p.out_mode == 1) {
-              reinterpret_cast<float*>(p.out)[idx] = fminf(fmaxf(y, p.out_lo), p.out_hi);
-            } else {
-              atomicAdd(reinterpret_cast<float*>(p.out) + idx, y);
-            }
+          for (int j = 0; j < 32; ++j) {
+            float y = fminf(fmaxf(fmaf(v[j], scale, bias), p.out_lo), p.out_hi);
+            if (p.act == 1) y = silu_f(bf16_round(y));
+            y = fminf(fmaxf(y, p.post_lo), p.post_hi);
+            st[j * kBlockO + q * 32 + lane] = __float2bfloat16_rn(y);
+          }
+        } else {
+          float* st = reinterpret_cast<float*>(stg);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float y = fmaf(v[j], scale, bias);
+            if (p.out_mode == 1) y = fminf(fmaxf(y, p.out_lo), p.out_hi);
+            st[j * kBlockO + q * 32 + lane] = y;
           }
         }
+        fence_proxy_async_smem();
+        epi_bar();
+        if (leader) {
+          if (p.out_mode == 2) {
+            tma_reduce_add_2d(&tm_out, stg, w.o0, w.t0 + c);
+          } else {
+            tma_store_2d(&tm_out, stg, w.o0, w.t0 + c);
+          }
+          bulk_commit();
+        }
+        ++chunks_issued;
       }
+      // accumulator drained: hand the TMEM buffer back to the MMA warp
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tmem_empty[b]);
     }
+    if (leader) bulk_wait_all();
   } else {
-    // ---------------- int8 -> bf16 converters (WINT8 only; warps 6..9)
+    // ---------------- int8 -> bf16 converters (WINT8 only; warps 6..13)
     if (WINT8) {
       const int ct = threadIdx.x - 192;
-      for (int i = 0; i < nkb; ++i) {
-        const int s = i % S;
-        const uint32_t ph = (i / S) & 1;
-        if (!mbar_wait(&full[s], ph, p.status)) break;
-        const uint8_t* raw = stage_raw(s);
-        uint8_t* dst = stage_a(s);
+      int it = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        const Unit w = unit_of(u, o_tiles, t_tiles, TN, p.kb_per_split, total_kb);
+        for (int i = 0; i < w.nkb; ++i, ++it) {
+          const int s = it % S;
+          const uint32_t ph = (it / S) & 1;
+          if (!mbar_wait(&full[s], ph, p.status)) {
+            ok = false;
+            break;
+          }
+          const uint8_t* raw = stage_raw(s);
+          uint8_t* dst = stage_a(s);
 #pragma unroll
-        for (int qd = 0; qd < 4; ++qd) {
-          const int c = ct + 128 * qd;  // 16-byte chunk id in the 128 x 64 B raw tile
-          const int row = c >> 2;
-          const int ch = c & 3;
-          const int4 r = *reinterpret_cast<const int4*>(raw + row * 64 + ch * 16);
-          int4 lo, hi;
-          convert_i8x16_to_bf16(r, lo, hi);
-          const int sw = row & 7;
-          *reinterpret_cast<int4*>(dst + row * 128 + (((2 * ch) ^ sw) << 4)) = lo;
-          *reinterpret_cast<int4*>(dst + row * 128 + (((2 * ch + 1) ^ sw) << 4)) = hi;
+          for (int qd = 0; qd < 2; ++qd) {
+            const int cidx = ct + 256 * qd;  // 16-byte chunk id in the 128 x 64 B raw tile
+            const int row = cidx >> 2;
+            const int ch = cidx & 3;
+            const int4 r = *reinterpret_cast<const int4*>(raw + row * 64 + ch * 16);
+            int4 lo, hi;
+            convert_i8x16_to_bf16(r, lo, hi);
+            const int sw = row & 7;
+            *reinterpret_cast<int4*>(dst + row * 128 + (((2 * ch) ^ sw) << 4)) = lo;
+            *reinterpret_cast<int4*>(dst + row * 128 + (((2 * ch + 1) ^ sw) << 4)) = hi;
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&conv[s]);
         }
-        fence_proxy_async_smem();
-        mbar_arrive(&conv[s]);
       }
     }
   }
@@ -245,11 +371,13 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 }
 
 template <int TN, bool WINT8>
-cudaError_t launch_gemm_t(const CUtensorMap& tw, const CUtensorMap& tx, const GemmParams& p,
-                          int m_cap, int splits, cudaStream_t stream) {
+cudaError_t launch_gemm_t(const GemmPlan& plan, const GemmParams& p, int splits, int num_sms,
+                          cudaStream_t stream) {
   using Cfg = GemmCfg<TN, WINT8>;
-  dim3 grid(p.O / kBlockO, (m_cap + TN - 1) / TN, splits);
-  gemm_wx_kernel<TN, WINT8><<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(tw, tx, p);
+  const int units = (plan.O / kBlockO) * ((plan.m_cap + TN - 1) / TN) * splits;
+  const int grid = units < num_sms ? units : num_sms;
+  gemm_wx_kernel<TN, WINT8>
+      <<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(plan.tm_w, plan.tm_x, plan.tm_out, p);
   return cudaGetLastError();
 }
 
@@ -257,6 +385,12 @@ template <int TN, bool WINT8>
 cudaError_t set_smem_attr() {
   return cudaFuncSetAttribute(gemm_wx_kernel<TN, WINT8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                               static_cast<int>(GemmCfg<TN, WINT8>::kSmemBytes));
+}
+
+int sm_count() {
+  int dev = 0, n = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n;
 }
 
 }  // namespace
@@ -281,8 +415,9 @@ int make_tensor_map_2d(CUtensorMap* map, const void* base, int elem_bytes, uint6
                        uint32_t box_outer, bool swizzle128) {
   auto enc = tensor_map_encoder();
   if (!enc) return -1;
-  const CUtensorMapDataType dt = elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                                 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  const CUtensorMapDataType dt = elem_bytes == 2   ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                 : elem_bytes == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                                   : CU_TENSOR_MAP_DATA_TYPE_UINT8;
   cuuint64_t dims[2] = {inner, outer};
   cuuint64_t strides[1] = {row_stride_bytes};
   cuuint32_t box[2] = {box_inner, box_outer};
@@ -301,14 +436,16 @@ int gemm_token_tile(int m_cap) {
   return 256;
 }
 
-int gemm_prepare(GemmPlan* plan, const void* w, bool w_int8, int O, int K, const void* x,
-                 int x_ld, int m_cap) {
-  if (O % kBlockO != 0 || K % kBlockK != 0 || x_ld % 8 != 0) return -3;
+int gemm_prepare(GemmPlan* plan, const void* w, bool w_int8, int O, int K, const void* x, int x_ld,
+                 int m_cap, void* out, int ld_out, int out_mode) {
+  if (O % kBlockO != 0 || K % kBlockK != 0 || x_ld % 8 != 0 || ld_out % 8 != 0 || m_cap < 1)
+    return -3;
   plan->O = O;
   plan->K = K;
   plan->w_int8 = w_int8;
   plan->m_cap = m_cap;
   plan->tn = gemm_token_tile(m_cap);
+  plan->out_mode = out_mode;
   int rc;
   if (w_int8) {
     rc = make_tensor_map_2d(&plan->tm_w, w, 1, K, O, static_cast<uint64_t>(K), kBlockK, kBlockO,
@@ -321,30 +458,39 @@ int gemm_prepare(GemmPlan* plan, const void* w, bool w_int8, int O, int K, const
   // The activation map covers exactly m_cap rows (TMA zero-fills rows past it).
   // A box may not exceed the tensor extent, so with fewer rows than the token
   // tile the box shrinks to m_cap rows; the tile's remaining shared-memory rows
-  // then hold stale data that only reaches output columns t >= m_cap, which the
-  // epilogue never stores.
+  // then hold stale data that only reaches output columns t >= m_cap, which are
+  // clipped by the output map.
   plan->x_box_rows = m_cap < plan->tn ? m_cap : plan->tn;
-  return make_tensor_map_2d(&plan->tm_x, x, 2, K, static_cast<uint64_t>(m_cap),
-                            static_cast<uint64_t>(x_ld) * 2, kBlockK,
-                            static_cast<uint32_t>(plan->x_box_rows), true);
+  rc = make_tensor_map_2d(&plan->tm_x, x, 2, K, static_cast<uint64_t>(m_cap),
+                          static_cast<uint64_t>(x_ld) * 2, kBlockK,
+                          static_cast<uint32_t>(plan->x_box_rows), true);
+  if (rc) return rc;
+  // Output map: [m_cap rows][ld_out], stores of 32-token x 128-feature boxes.
+  // Rows t >= m_cap are clipped by TMA; rows in [M, m_cap) receive values of
+  // columns the kernel computed from stale activation rows -- never read.
+  const int ebytes = out_mode == 0 ? 2 : 4;
+  plan->out_box_rows = m_cap < kChunk ? m_cap : kChunk;
+  return make_tensor_map_2d(&plan->tm_out, out, ebytes, static_cast<uint64_t>(O),
+                            static_cast<uint64_t>(m_cap), static_cast<uint64_t>(ld_out) * ebytes,
+                            kBlockO, static_cast<uint32_t>(plan->out_box_rows), false);
 }
 
 cudaError_t gemm_launch(const GemmPlan& plan, GemmParams p, int splits, cudaStream_t stream) {
   p.O = plan.O;
   p.K = plan.K;
   p.b_tx_bytes = static_cast<uint32_t>(plan.x_box_rows) * kBlockK * 2;
+  if (p.out_mode != plan.out_mode) return cudaErrorInvalidValue;
   const int total_kb = plan.K / kBlockK;
   if (splits < 1) splits = 1;
   if (splits > total_kb) splits = total_kb;
   p.kb_per_split = (total_kb + splits - 1) / splits;
   splits = (total_kb + p.kb_per_split - 1) / p.kb_per_split;
   if (splits > 1 && p.out_mode != 2) return cudaErrorInvalidValue;
-#define LB_GEMM_CASE(TNV)                                                              \
-  case TNV:                                                                            \
-    return plan.w_int8 ? launch_gemm_t<TNV, true>(plan.tm_w, plan.tm_x, p, plan.m_cap, \
-                                                  splits, stream)                      \
-                       : launch_gemm_t<TNV, false>(plan.tm_w, plan.tm_x, p, plan.m_cap, \
-                                                   splits, stream);
+  const int sms = sm_count();
+#define LB_GEMM_CASE(TNV)                                                                  \
+  case TNV:                                                                                \
+    return plan.w_int8 ? launch_gemm_t<TNV, true>(plan, p, splits, sms, stream)            \
+                       : launch_gemm_t<TNV, false>(plan, p, splits, sms, stream);
   switch (plan.tn) {
     LB_GEMM_CASE(32)
     LB_GEMM_CASE(64)
@@ -356,15 +502,25 @@ cudaError_t gemm_launch(const GemmPlan& plan, GemmParams p, int splits, cudaStre
 #undef LB_GEMM_CASE
 }
 
-int gemm_pick_splits(const GemmPlan& plan, int num_sms) {
-  const int tiles = (plan.O / kBlockO) * ((plan.m_cap + plan.tn - 1) / plan.tn);
-  const int total_kb = plan.K / kBlockK;
-  if (tiles >= num_sms) return 1;
-  int splits = (num_sms + tiles - 1) / tiles;
-  // keep at least 4 k-blocks per split so the pipeline fills
-  const int max_splits = total_kb / 4 > 0 ? total_kb / 4 : 1;
-  if (splits > max_splits) splits = max_splits;
-  return splits < 1 ? 1 : splits;
+int gemm_pick_splits(int O, int K, int m_cap, int num_sms) {
+  const int tn = gemm_token_tile(m_cap);
+  const int tiles = (O / kBlockO) * ((m_cap + tn - 1) / tn);
+  const int total_kb = K / kBlockK;
+  // Choose the split count that best fills whole waves of SMs: efficiency =
+  // units / (waves * SMs).  Each extra split costs an fp32 partial-sum
+  // reduction, so a split must gain at least 8% and keep >= 6 k-blocks.
+  int best = 1;
+  double best_eff = static_cast<double>(tiles) / (((tiles + num_sms - 1) / num_sms) * num_sms);
+  for (int s = 2; s <= 16; ++s) {
+    if (total_kb / s < 6) break;
+    const int units = tiles * s;
+    const double eff = static_cast<double>(units) / (((units + num_sms - 1) / num_sms) * num_sms);
+    if (eff > best_eff + 0.08) {
+      best = s;
+      best_eff = eff;
+    }
+  }
+  return best;
 }
 
 }  // namespace lb

@@ -10,11 +10,6 @@
 //                      next GEMM's bf16 input, in one pass
 //                      (transformers modeling_gemma4.py:390-408, 513-537;
 //                      streaming_conformer.py:777, 853-860)
-//   attention_kernel   chunked local attention of the 2 new tokens over each
-//                      session's K/V ring read in place: content + relative-
-//                      position logits, 50-softcap, window/validity mask,
-//                      fp32 softmax, weighted V; stages the 2 new K/V entries
-//                      (streaming_conformer.py:778-829, modeling_gemma4.py:209-314)
 //   lconv_kernel       GLU -> causal depthwise conv (k=5) over the conv-state
 //                      ring -> clamp -> RMSNorm -> SiLU -> bf16; stages the 2 new
 //                      GLU rows (streaming_conformer.py:830-852, modeling_gemma4.py:444-482)
@@ -140,171 +135,6 @@ __global__ void __launch_bounds__(256) row_fused_kernel(RowFusedDev a) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) xv[i] = fminf(fmaxf(xv[i], a.in_lo), a.in_hi);
     store8_bf16(a.xa + base, xv);
-  }
-}
-
-// ------------------------------------------------------------- attention
-struct AttnDev {
-  const int* counts;
-  const int *row_slot, *row_mask;
-  const SlotMeta* row_meta;
-  const __nv_bfloat16* qkv;  // [tok][3d]
-  __nv_bfloat16 *kc, *vc;    // [S][L][16][d]
-  __nv_bfloat16* out;        // [tok][d]
-  const float* q_mult;       // [hd]
-  const float* rel;          // [13][d]
-  int layer, layers, d, hd;
-  float k_scale, softcap, invalid;
-  float in_lo, in_hi;  // attention.post input clamp
-};
-
-// One CTA per batch row, one warp per head.  Each lane owns head-dim pairs
-// e = 2*lane + 64*r (r < hd/64).
-template <int NP>  // NP = hd / 64 pairs per lane
-__global__ void __launch_bounds__(512) attention_kernel(AttnDev a) {
-  const int row = blockIdx.x;
-  if (row >= a.counts[0]) return;
-  const int head = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int slot = a.row_slot[row];
-  const SlotMeta m = a.row_meta[row];
-  const int mask = a.row_mask[row];
-  const int d = a.d;
-  const size_t ring_base = (static_cast<size_t>(slot) * a.layers + a.layer) * kRing * d;
-  const int hoff = head * a.hd;
-
-  float q[2][2 * NP], kn[2][2 * NP], vn[2][2 * NP], qm[2 * NP];
-#pragma unroll
-  for (int r = 0; r < NP; ++r) {
-    const int e = 2 * lane + 64 * r;
-    qm[2 * r] = a.q_mult[e];
-    qm[2 * r + 1] = a.q_mult[e + 1];
-#pragma unroll
-    for (int t = 0; t < 2; ++t) {
-      const __nv_bfloat16* src = a.qkv + (static_cast<size_t>(row) * 2 + t) * 3 * d + hoff + e;
-      const float2 qv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src));
-      const float2 kv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src + d));
-      const float2 vv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src + 2 * d));
-      q[t][2 * r] = qv.x * qm[2 * r];
-      q[t][2 * r + 1] = qv.y * qm[2 * r + 1];
-      kn[t][2 * r] = kv.x;
-      kn[t][2 * r + 1] = kv.y;
-      vn[t][2 * r] = vv.x;
-      vn[t][2 * r + 1] = vv.y;
-    }
-  }
-  // logits over 15 keys: j < 13 cached (ring entry pos + j), j = 13, 14 the new tokens
-  float logit[2][15];
-  const int first_real = kCached - m.fill;  // cached entries before this were never written
-  for (int j = 0; j < 15; ++j) {
-    float kv[2 * NP];
-    if (j < kCached) {
-      const int idx = (m.pos + j) & (kRing - 1);
-      const __nv_bfloat16* src = a.kc + ring_base + static_cast<size_t>(idx) * d + hoff;
-#pragma unroll
-      for (int r = 0; r < NP; ++r) {
-        float2 f = make_float2(0.f, 0.f);
-        if (j >= first_real)
-          f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src + 2 * lane + 64 * r));
-        kv[2 * r] = f.x;
-        kv[2 * r + 1] = f.y;
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 2 * NP; ++i) kv[i] = kn[j - kCached][i];
-    }
-#pragma unroll
-    for (int t = 0; t < 2; ++t) {
-      const int dist = j < kCached ? (kCached - j + t) : (t - (j - kCached));
-      const int ridx = 12 - min(max(dist, 0), 12);
-      const float* rel = a.rel + static_cast<size_t>(ridx) * d + hoff;
-      float acc = 0.f;
-#pragma unroll
-      for (int r = 0; r < NP; ++r) {
-        const int e = 2 * lane + 64 * r;
-        acc = fmaf(q[t][2 * r], fmaf(kv[2 * r], a.k_scale, 0.f) + rel[e], acc);
-        acc = fmaf(q[t][2 * r + 1], fmaf(kv[2 * r + 1], a.k_scale, 0.f) + rel[e + 1], acc);
-      }
-      logit[t][j] = warp_sum(acc);
-    }
-  }
-  // softcap, mask, softmax (fp32), then weighted values
-  float p[2][15];
-#pragma unroll
-  for (int t = 0; t < 2; ++t) {
-    float mx = -INFINITY;
-#pragma unroll
-    for (int j = 0; j < 15; ++j) {
-      const int dist = j < kCached ? (kCached - j + t) : (t - (j - kCached));
-      bool ok = dist >= 0 && dist < 12;
-      if (j < kCached) {
-        ok = ok && ((m.valid_bits >> ((m.pos + j) & (kRing - 1))) & 1);
-      } else {
-        ok = ok && ((mask >> (4 * (j - kCached))) & 1);
-      }
-      float l = tanhf(logit[t][j] / a.softcap) * a.softcap;
-      l = ok ? l : a.invalid;
-      p[t][j] = l;
-      mx = fmaxf(mx, l);
-    }
-    float sum = 0.f;
-#pragma unroll
-    for (int j = 0; j < 15; ++j) {
-      p[t][j] = expf(p[t][j] - mx);
-      sum += p[t][j];
-    }
-    const float inv = 1.0f / sum;
-#pragma unroll
-    for (int j = 0; j < 15; ++j) p[t][j] *= inv;
-  }
-  float o[2][2 * NP];
-#pragma unroll
-  for (int t = 0; t < 2; ++t)
-#pragma unroll
-    for (int i = 0; i < 2 * NP; ++i) o[t][i] = 0.f;
-  for (int j = 0; j < 15; ++j) {
-    float vv[2 * NP];
-    if (j < kCached) {
-      const int idx = (m.pos + j) & (kRing - 1);
-      const __nv_bfloat16* src = a.vc + ring_base + static_cast<size_t>(idx) * d + hoff;
-      const bool live = j >= first_real && (p[0][j] != 0.f || p[1][j] != 0.f);
-#pragma unroll
-      for (int r = 0; r < NP; ++r) {
-        float2 f = make_float2(0.f, 0.f);
-        if (live)
-          f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src + 2 * lane + 64 * r));
-        vv[2 * r] = f.x;
-        vv[2 * r + 1] = f.y;
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 2 * NP; ++i) vv[i] = vn[j - kCached][i];
-    }
-#pragma unroll
-    for (int t = 0; t < 2; ++t)
-#pragma unroll
-      for (int i = 0; i < 2 * NP; ++i) o[t][i] = fmaf(p[t][j], vv[i], o[t][i]);
-  }
-#pragma unroll
-  for (int t = 0; t < 2; ++t) {
-    __nv_bfloat16* dst = a.out + (static_cast<size_t>(row) * 2 + t) * d + hoff;
-#pragma unroll
-    for (int r = 0; r < NP; ++r)
-      *reinterpret_cast<__nv_bfloat162*>(dst + 2 * lane + 64 * r) =
-          __floats2bfloat162_rn(fminf(fmaxf(o[t][2 * r], a.in_lo), a.in_hi),
-                                fminf(fmaxf(o[t][2 * r + 1], a.in_lo), a.in_hi));
-  }
-  // stage the two new K/V entries at ring positions pos+13, pos+14
-#pragma unroll
-  for (int t = 0; t < 2; ++t) {
-    const int idx = (m.pos + kCached + t) & (kRing - 1);
-    __nv_bfloat16* kd = a.kc + ring_base + static_cast<size_t>(idx) * d + hoff;
-    __nv_bfloat16* vd = a.vc + ring_base + static_cast<size_t>(idx) * d + hoff;
-#pragma unroll
-    for (int r = 0; r < NP; ++r) {
-      const int e = 2 * lane + 64 * r;
-      *reinterpret_cast<__nv_bfloat162*>(kd + e) = __floats2bfloat162_rn(kn[t][2 * r], kn[t][2 * r + 1]);
-      *reinterpret_cast<__nv_bfloat162*>(vd + e) = __floats2bfloat162_rn(vn[t][2 * r], vn[t][2 * r + 1]);
-    }
   }
 }
 
@@ -505,38 +335,6 @@ cudaError_t launch_row_fused(Ctx& c, int tok_cap, const RowFusedArgs& r, cudaStr
   a.xa = r.xa;
   a.dbg = r.dbg;
   row_fused_kernel<<<tok_cap, c.cfg.hidden / 8, 0, s>>>(a);
-  return cudaGetLastError();
-}
-
-cudaError_t launch_attention(Ctx& c, int layer, int rows_cap, cudaStream_t s) {
-  AttnDev a;
-  a.counts = c.dev_counts;
-  a.row_slot = c.row_slot;
-  a.row_mask = c.row_mask;
-  a.row_meta = c.row_meta;
-  a.qkv = c.qkv;
-  a.kc = c.kv_k;
-  a.vc = c.kv_v;
-  a.out = c.att;
-  a.q_mult = c.w.layers[layer].q_mult;
-  a.rel = c.w.layers[layer].rel_keys;
-  a.layer = layer;
-  a.layers = c.cfg.layers;
-  a.d = c.cfg.hidden;
-  a.hd = c.hd;
-  a.k_scale = static_cast<float>(std::log1p(std::exp(1.0)) / std::log(2.0));
-  a.softcap = c.cfg.softcap;
-  a.invalid = c.cfg.invalid_logit;
-  a.in_lo = c.w.layers[layer].clip[5][0];
-  a.in_hi = c.w.layers[layer].clip[5][1];
-  const int threads = 32 * c.cfg.heads;
-  switch (c.hd / 64) {
-    case 1: attention_kernel<1><<<rows_cap, threads, 0, s>>>(a); break;
-    case 2: attention_kernel<2><<<rows_cap, threads, 0, s>>>(a); break;
-    case 3: attention_kernel<3><<<rows_cap, threads, 0, s>>>(a); break;
-    case 4: attention_kernel<4><<<rows_cap, threads, 0, s>>>(a); break;
-    default: return cudaErrorInvalidValue;
-  }
   return cudaGetLastError();
 }
 

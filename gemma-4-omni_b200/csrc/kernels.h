@@ -34,8 +34,11 @@ struct GemmParams {
 struct GemmPlan {
   CUtensorMap tm_w;
   CUtensorMap tm_x;
+  CUtensorMap tm_out;
   int O = 0, K = 0, m_cap = 0, tn = 0;
-  int x_box_rows = 0;  // rows per activation TMA box: min(tn, m_cap)
+  int x_box_rows = 0;    // rows per activation TMA box: min(tn, m_cap)
+  int out_box_rows = 0;  // rows per output TMA box: min(32, m_cap)
+  int out_mode = 0;
   bool w_int8 = false;
 };
 
@@ -43,11 +46,13 @@ int make_tensor_map_2d(CUtensorMap* map, const void* base, int elem_bytes, uint6
                        uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
                        uint32_t box_outer, bool swizzle128);
 int gemm_token_tile(int m_cap);
-// Encodes the tensor maps for W ([O,K] bf16 or int8) and X ([m_cap,K], row
-// stride x_ld elements).  X needs m_cap rows; TMA zero-fills the rest.
+// Encodes the tensor maps for W ([O,K] bf16 or int8), X ([m_cap,K], row stride
+// x_ld elements; TMA zero-fills rows past m_cap) and the output ([m_cap, ld_out],
+// bf16 for out_mode 0, fp32 otherwise; stores past m_cap are clipped).
 int gemm_prepare(GemmPlan* plan, const void* w, bool w_int8, int O, int K, const void* x, int x_ld,
-                 int m_cap);
+                 int m_cap, void* out, int ld_out, int out_mode);
 cudaError_t gemm_launch(const GemmPlan& plan, GemmParams p, int splits, cudaStream_t stream);
-int gemm_pick_splits(const GemmPlan& plan, int num_sms);
+// K-split count that fills the SMs for an [m_cap x O] output with K reduction.
+int gemm_pick_splits(int O, int K, int m_cap, int num_sms);
 
 }  // namespace lb

@@ -53,8 +53,9 @@ def test_gemm_fp32_out_matches_torch(lib, M, int8):
 @pytest.mark.parametrize("int8", [False, True])
 def test_gemm_bf16_silu_bias_matches_torch(lib, M, int8):
     out, ref = run_gemm(lib, M, 6144, 1536, int8, 0, 1, 1, True, seed=100 + M)
-    # bf16 output rounding: half an ulp of bf16 (2^-8 relative) plus fp32 reorder
-    torch.testing.assert_close(out, ref, rtol=8e-3, atol=1e-3)
+    # bf16 output: the result is rounded once (<= 1 ulp = 2^-7 relative) and the
+    # pre-SiLU bf16 rounding may flip by one ulp under fp32 summation order
+    torch.testing.assert_close(out, ref, rtol=1.6e-2, atol=1e-3)
 
 
 @pytest.mark.parametrize("splits", [2, 7, 24])
