@@ -43,6 +43,7 @@ using namespace lb;
 namespace lb {
 cudaError_t gemm_init_attributes();
 cudaError_t frontend_init_attributes();
+cudaError_t attention_init_attributes();
 }  // namespace lb
 
 namespace {
@@ -400,6 +401,13 @@ int make_op(Ctx& c, GemmOp& op, void* w, const __half* scale, int O, int K, cons
   p.post_hi = post_hi;
   const bool finite_out = std::isfinite(p.out_lo) || std::isfinite(p.out_hi);
   op.splits = finite_out && out_kind == 1 ? 1 : gemm_pick_splits(O, K, tok_cap, c.num_sms);
+  if (out_kind == 0) {
+    // A split bf16 output goes through an fp32 partial-sum buffer and a finalize
+    // pass; worth it only while the tiles cannot fill half of the SMs.
+    const int tn = gemm_token_tile(tok_cap);
+    const int tiles = (O / 128) * ((tok_cap + tn - 1) / tn);
+    if (tiles * 2 >= c.num_sms) op.splits = 1;
+  }
   if (op.splits > 1) {
     p.out_mode = 2;
     p.out = out_kind == 0 ? static_cast<void*>(c.wide_acc) : out;
@@ -623,7 +631,8 @@ int lb_create(const lb_config* cfg, lb_ctx** out_ctx) {
   c.max_handles = cfg->max_handles;
   if (cudaGetDevice(&c.device) != cudaSuccess) return LB_ERR_CUDA;
   cudaDeviceGetAttribute(&c.num_sms, cudaDevAttrMultiProcessorCount, c.device);
-  if (gemm_init_attributes() != cudaSuccess || frontend_init_attributes() != cudaSuccess)
+  if (gemm_init_attributes() != cudaSuccess || frontend_init_attributes() != cudaSuccess ||
+      attention_init_attributes() != cudaSuccess)
     return LB_ERR_CUDA;
   // weights
   c.weight_bytes = layout_weights(x.get(), nullptr, false);
@@ -736,6 +745,18 @@ int lb_set_tensor(lb_ctx* x, const char* name, const void* host, int dtype, int6
                 __float2bfloat16(w[((co * 128 + ci) * 3 + i) * 3 + j]);
     if (cudaMemcpy(t.dst, out.data(), out.size() * 2, cudaMemcpyHostToDevice) != cudaSuccess)
       return LB_ERR_CUDA;
+    t.set = true;
+    return LB_OK;
+  }
+  const std::string dw_suffix = ".lconv1d.depthwise_conv1d.weight";
+  if (n.size() > dw_suffix.size() && n.compare(n.size() - dw_suffix.size(), dw_suffix.size(), dw_suffix) == 0) {
+    // [d][1][5] -> tap-major [5][d] so the conv kernel loads each tap as vectors
+    const float* w = static_cast<const float*>(host);
+    const int d = c.cfg.hidden;
+    std::vector<float> tr(static_cast<size_t>(d) * 5);
+    for (int e = 0; e < d; ++e)
+      for (int k = 0; k < 5; ++k) tr[static_cast<size_t>(k) * d + e] = w[e * 5 + k];
+    if (cudaMemcpy(t.dst, tr.data(), tr.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess) return LB_ERR_CUDA;
     t.set = true;
     return LB_OK;
   }

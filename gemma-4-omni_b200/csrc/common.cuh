@@ -209,7 +209,10 @@ __host__ __device__ constexpr uint32_t umma_idesc_bf16(int m, int n) {
 __device__ __forceinline__ float bf16_round(float x) {
   return __bfloat162float(__float2bfloat16_rn(x));
 }
-__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
+// SiLU with the fast exponential and division intrinsics: the result is
+// rounded to bf16 right after, far coarser than their few-ulp error.  For very
+// negative x, 1 + e^-x overflows and the quotient flushes to -0 (true value ~0).
+__device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

@@ -51,13 +51,13 @@ constexpr uint32_t kStagingBytes = kChunk * kBlockO * 4;  // one fp32 staging bu
 template <int TN, bool WINT8>
 struct GemmCfg {
   static constexpr uint32_t kBBytes = TN * kBlockK * 2;
-  static constexpr uint32_t kStageBytes = kABytes + kBBytes + (WINT8 ? kRawBytes : 0);
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
   // operand ring + 2 staging buffers within 224 KB (the 227 KB opt-in limit
   // leaves room for barriers and the 1 KB alignment slack)
   static constexpr int kStages = (224 * 1024 - 2 * kStagingBytes) / kStageBytes > 8
                                      ? 8
                                      : (224 * 1024 - 2 * kStagingBytes) / kStageBytes;
-  static constexpr uint32_t kBarBytes = (3 * kStages + 4) * 8 + 16;
+  static constexpr uint32_t kBarBytes = (4 * kStages + 4) * 8 + 16;
   static constexpr uint32_t kSmemBytes =
       kStages * kStageBytes + 2 * kStagingBytes + kBarBytes + 1024;
   static constexpr int kThreads = WINT8 ? 448 : 192;
@@ -155,15 +155,17 @@ __global__ void __launch_bounds__(GemmCfg<TN, WINT8>::kThreads, 1)
 
   auto stage_a = [&](int s) { return smem + s * Cfg::kStageBytes; };
   auto stage_b = [&](int s) { return smem + s * Cfg::kStageBytes + kABytes; };
-  auto stage_raw = [&](int s) { return smem + s * Cfg::kStageBytes + kABytes + Cfg::kBBytes; };
+  // int8 weights land in the upper half of their stage's bf16 A tile
+  auto stage_raw = [&](int s) { return smem + s * Cfg::kStageBytes + kRawBytes; };
   uint8_t* staging = smem + S * Cfg::kStageBytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(staging + 2 * kStagingBytes);
   uint64_t* full = bars;
   uint64_t* empty = bars + S;
   uint64_t* conv = bars + 2 * S;
-  uint64_t* tmem_full = bars + 3 * S;       // [2]
-  uint64_t* tmem_empty = bars + 3 * S + 2;  // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * S + 4);
+  uint64_t* rawrd = bars + 3 * S;           // int8: every converter warp has read the raw tile
+  uint64_t* tmem_full = bars + 4 * S;       // [2]
+  uint64_t* tmem_empty = bars + 4 * S + 2;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4 * S + 4);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -172,7 +174,10 @@ __global__ void __launch_bounds__(GemmCfg<TN, WINT8>::kThreads, 1)
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
-      if (WINT8) mbar_init(&conv[s], 8);
+      if (WINT8) {
+        mbar_init(&conv[s], 8);
+        mbar_init(&rawrd[s], 8);
+      }
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tmem_full[b], 1);
@@ -325,16 +330,29 @@ __global__ void __launch_bounds__(GemmCfg<TN, WINT8>::kThreads, 1)
             ok = false;
             break;
           }
+          // The int8 tile sits in the upper half of the bf16 tile it widens into:
+          // read every raw chunk first, meet on rawrd[s], then write.
           const uint8_t* raw = stage_raw(s);
           uint8_t* dst = stage_a(s);
+          int4 r[2];
 #pragma unroll
           for (int qd = 0; qd < 2; ++qd) {
             const int cidx = ct + 256 * qd;  // 16-byte chunk id in the 128 x 64 B raw tile
+            r[qd] = *reinterpret_cast<const int4*>(raw + (cidx >> 2) * 64 + (cidx & 3) * 16);
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&rawrd[s]);
+          if (!mbar_wait(&rawrd[s], ph, p.status)) {
+            ok = false;
+            break;
+          }
+#pragma unroll
+          for (int qd = 0; qd < 2; ++qd) {
+            const int cidx = ct + 256 * qd;
             const int row = cidx >> 2;
             const int ch = cidx & 3;
-            const int4 r = *reinterpret_cast<const int4*>(raw + row * 64 + ch * 16);
             int4 lo, hi;
-            convert_i8x16_to_bf16(r, lo, hi);
+            convert_i8x16_to_bf16(r[qd], lo, hi);
             const int sw = row & 7;
             *reinterpret_cast<int4*>(dst + row * 128 + (((2 * ch) ^ sw) << 4)) = lo;
             *reinterpret_cast<int4*>(dst + row * 128 + (((2 * ch + 1) ^ sw) << 4)) = hi;

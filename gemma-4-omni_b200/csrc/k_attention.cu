@@ -10,16 +10,17 @@
 //   logit = 50 tanh(logit / 50); masked to -1e9 outside 0 <= dist < 12 or for
 //   invalid tokens; fp32 softmax; out = sum p_j v_j.
 //
-// Layout: one CTA per batch row (session), one warp per head.  For the logits
-// a lane owns one (query, key) pair -- lanes 0..14 query 0, lanes 16..30 query
-// 1 -- and computes its dot product privately from its own K row (16-byte
-// loads, all independent), so no per-key warp reduction is needed.  Keys that
-// are outside the window of the lane's query are never loaded (cached keys 0
-// and 1 are outside both windows).  The softmax reduces within each 16-lane
-// half; then lanes switch to owning head dimensions and accumulate p_j * v_j,
-// loading only values with a non-zero weight.  If every key of a query is
+// Layout: one CTA per batch row (session), one warp per head.  Lanes own head
+// dimensions for every load, so K rows, V rows and relative-key rows are read
+// with whole-warp coalesced accesses; each lane forms partial dot products for
+// the 13 reachable keys and the 12 window distances, and a padded shared-memory
+// transpose sums them.  Lanes then own (query, key) pairs -- lanes 0..14 query
+// 0, lanes 16..30 query 1 -- for the logits and the softmax, which reduces
+// within each 16-lane half.  Cached keys 0 and 1 lie outside both windows and
+// invalid keys are masked, so neither is loaded.  If every key of a query is
 // masked, all logits equal the invalid value and the softmax is uniform over
-// the 15 keys, exactly as in the reference.
+// the 15 keys, exactly as in the reference; values are loaded only for keys
+// with a non-zero weight.
 #include "common.cuh"
 #include "listener.h"
 
@@ -44,8 +45,10 @@ struct AttnDev {
 
 template <int HD>
 __global__ void __launch_bounds__(512) attention_kernel(AttnDev a) {
-  constexpr int NP = HD / 64;  // bf16 pairs per lane when lanes own dimensions
-  extern __shared__ float qs[];  // [heads][2][HD]
+  constexpr int NP = HD / 64;  // bf16 pairs per lane (lanes own head dimensions)
+  // per warp: 52 partial sums x 33 (padded) + 52 totals
+  constexpr int kParts = 52, kPad = 33;
+  extern __shared__ float smem_att[];
   const int row = blockIdx.x;
   if (row >= a.counts[0]) return;
   const int head = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -56,25 +59,77 @@ __global__ void __launch_bounds__(512) attention_kernel(AttnDev a) {
   const size_t ring_base = (static_cast<size_t>(slot) * a.layers + a.layer) * kRing * d;
   const int hoff = head * HD;
   const __nv_bfloat16* qkv0 = a.qkv + static_cast<size_t>(row) * 2 * 3 * d;
-  float* q_smem = qs + head * 2 * HD;
+  float* part = smem_att + head * (kParts * kPad + kParts);
+  float* tot = part + kParts * kPad;
 
-  // scaled queries of this head into shared memory
+  // scaled queries (registers), lane dims e = 2*lane + 64*r
+  float q[2][2 * NP];
 #pragma unroll
   for (int t = 0; t < 2; ++t)
 #pragma unroll
     for (int r = 0; r < NP; ++r) {
       const int e = 2 * lane + 64 * r;
-      const float2 qv = __bfloat1622float2(
-          *reinterpret_cast<const __nv_bfloat162*>(qkv0 + t * 3 * d + hoff + e));
-      q_smem[t * HD + e] = qv.x * a.q_mult[e];
-      q_smem[t * HD + e + 1] = qv.y * a.q_mult[e + 1];
+      const float2 qv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(qkv0 + t * 3 * d + hoff + e));
+      q[t][2 * r] = qv.x * a.q_mult[e];
+      q[t][2 * r + 1] = qv.y * a.q_mult[e + 1];
     }
+  // ---- partial dot products, all loads coalesced across the warp.
+  // part[2*i + t]       : q_t . k_{2+i}            keys j = 2..14 (i = 0..12)
+  // part[26 + 2*dist + t]: q_t . relK[12 - dist]    dist = 0..11
+  // Cached keys 0 and 1 lie outside both windows; invalid cached keys are
+  // masked whatever their logit, so neither is loaded.
+#pragma unroll
+  for (int i = 0; i < 13; ++i) {
+    const int j = 2 + i;
+    float s0 = 0.f, s1 = 0.f;
+    bool need;
+    const __nv_bfloat16* krow;
+    if (j < kCached) {
+      const int idx = (m.pos + j) & (kRing - 1);
+      need = (m.valid_bits >> idx) & 1;
+      krow = a.kc + ring_base + static_cast<size_t>(idx) * d + hoff;
+    } else {
+      need = (mask >> (4 * (j - kCached))) & 1;
+      krow = qkv0 + (j - kCached) * 3 * d + d + hoff;
+    }
+    if (need) {
+#pragma unroll
+      for (int r = 0; r < NP; ++r) {
+        const float2 k = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(krow + 2 * lane + 64 * r));
+        s0 = fmaf(q[0][2 * r], k.x, fmaf(q[0][2 * r + 1], k.y, s0));
+        s1 = fmaf(q[1][2 * r], k.x, fmaf(q[1][2 * r + 1], k.y, s1));
+      }
+    }
+    part[(2 * i) * kPad + lane] = s0;
+    part[(2 * i + 1) * kPad + lane] = s1;
+  }
+#pragma unroll
+  for (int dist = 0; dist < 12; ++dist) {
+    const float* rrow = a.rel + static_cast<size_t>(12 - dist) * d + hoff;
+    float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+    for (int r = 0; r < NP; ++r) {
+      const float2 rv = __ldg(reinterpret_cast<const float2*>(rrow + 2 * lane + 64 * r));
+      s0 = fmaf(q[0][2 * r], rv.x, fmaf(q[0][2 * r + 1], rv.y, s0));
+      s1 = fmaf(q[1][2 * r], rv.x, fmaf(q[1][2 * r + 1], rv.y, s1));
+    }
+    part[(26 + 2 * dist) * kPad + lane] = s0;
+    part[(26 + 2 * dist + 1) * kPad + lane] = s1;
+  }
+  __syncwarp();
+  // transpose-reduce: lane l totals rows l and l + 32
+  for (int rr = lane; rr < 50; rr += 32) {
+    float s = 0.f;
+#pragma unroll 8
+    for (int c = 0; c < 32; ++c) s += part[rr * kPad + c];
+    tot[rr] = s;
+  }
   __syncwarp();
 
-  // ---- logits: lane -> (query t, key j)
+  // ---- logits: lane -> (query t, key j); lanes 15 and 31 hold no key
   const int t = lane >> 4;
   const int j = lane & 15;
-  float logit = -INFINITY;  // lanes 15 and 31 hold no key
+  float logit = -INFINITY;
   if (j < 15) {
     const int dist = j < kCached ? (kCached - j + t) : (t - (j - kCached));
     bool ok = dist >= 0 && dist < 12;
@@ -84,36 +139,13 @@ __global__ void __launch_bounds__(512) attention_kernel(AttnDev a) {
       ok = ok && ((mask >> (4 * (j - kCached))) & 1);
     }
     logit = a.invalid;
-    if (ok) {
-      const __nv_bfloat16* krow =
-          j < kCached ? a.kc + ring_base + static_cast<size_t>((m.pos + j) & (kRing - 1)) * d + hoff
-                      : qkv0 + (j - kCached) * 3 * d + d + hoff;
-      const float* rel = a.rel + static_cast<size_t>(12 - min(max(dist, 0), 12)) * d + hoff;
-      const float* qrow = q_smem + t * HD;
-      float acc = 0.f;
-#pragma unroll 4
-      for (int e = 0; e < HD; e += 8) {
-        const int4 kr = *reinterpret_cast<const int4*>(krow + e);
-        const __nv_bfloat162* kp = reinterpret_cast<const __nv_bfloat162*>(&kr);
-        const float4 r0 = __ldg(reinterpret_cast<const float4*>(rel + e));
-        const float4 r1 = __ldg(reinterpret_cast<const float4*>(rel + e + 4));
-        const float4 q0 = *reinterpret_cast<const float4*>(qrow + e);
-        const float4 q1 = *reinterpret_cast<const float4*>(qrow + e + 4);
-        const float2 k0 = __bfloat1622float2(kp[0]), k1 = __bfloat1622float2(kp[1]);
-        const float2 k2 = __bfloat1622float2(kp[2]), k3 = __bfloat1622float2(kp[3]);
-        acc = fmaf(q0.x, fmaf(k0.x, a.k_scale, r0.x), acc);
-        acc = fmaf(q0.y, fmaf(k0.y, a.k_scale, r0.y), acc);
-        acc = fmaf(q0.z, fmaf(k1.x, a.k_scale, r0.z), acc);
-        acc = fmaf(q0.w, fmaf(k1.y, a.k_scale, r0.w), acc);
-        acc = fmaf(q1.x, fmaf(k2.x, a.k_scale, r1.x), acc);
-        acc = fmaf(q1.y, fmaf(k2.y, a.k_scale, r1.y), acc);
-        acc = fmaf(q1.z, fmaf(k3.x, a.k_scale, r1.z), acc);
-        acc = fmaf(q1.w, fmaf(k3.y, a.k_scale, r1.w), acc);
-      }
+    if (ok) {  // ok implies j >= 2 and 0 <= dist < 12
+      const float acc = fmaf(tot[2 * (j - 2) + t], a.k_scale, tot[26 + 2 * dist + t]);
       logit = tanhf(acc / a.softcap) * a.softcap;
     }
   }
-  // ---- softmax within each 16-lane half (one query per half)
+  // ---- softmax within each 16-lane half (one query per half).  If every key of
+  // a query is masked, all 15 logits equal the invalid value: uniform weights.
   float mx = logit;
 #pragma unroll
   for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
@@ -171,7 +203,20 @@ __global__ void __launch_bounds__(512) attention_kernel(AttnDev a) {
   }
 }
 
+size_t attention_smem_bytes(int heads) { return static_cast<size_t>(heads) * (52 * 33 + 52) * sizeof(float); }
+
 }  // namespace
+
+// Dynamic shared memory above 48 KB must be enabled per kernel instance, once
+// per device and before any graph capture.
+cudaError_t attention_init_attributes() {
+  const int bytes = static_cast<int>(attention_smem_bytes(16));
+  cudaError_t e = cudaFuncSetAttribute(attention_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(attention_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(attention_kernel<192>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(attention_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  return e;
+}
 
 cudaError_t launch_attention(Ctx& c, int layer, int rows_cap, cudaStream_t s) {
   AttnDev a;
@@ -194,7 +239,7 @@ cudaError_t launch_attention(Ctx& c, int layer, int rows_cap, cudaStream_t s) {
   a.in_lo = c.w.layers[layer].clip[5][0];
   a.in_hi = c.w.layers[layer].clip[5][1];
   const int threads = 32 * c.cfg.heads;
-  const size_t smem = static_cast<size_t>(c.cfg.heads) * 2 * c.hd * sizeof(float);
+  const size_t smem = attention_smem_bytes(c.cfg.heads);
   switch (c.hd) {
     case 64: attention_kernel<64><<<rows_cap, threads, smem, s>>>(a); break;
     case 128: attention_kernel<128><<<rows_cap, threads, smem, s>>>(a); break;

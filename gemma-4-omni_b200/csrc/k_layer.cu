@@ -145,7 +145,7 @@ struct LconvDev {
   const SlotMeta* row_meta;
   const __nv_bfloat16* gl;   // [tok][2d]
   __nv_bfloat16* ring;       // [S][L][8][d]
-  const float* dw;           // [d][5]
+  const float* dw;           // [5][d] tap-major
   const float* norm_w;       // [d]
   __nv_bfloat16* xa;         // [tok][d]
   int layer, layers, d;
@@ -183,11 +183,14 @@ __global__ void __launch_bounds__(256) lconv_kernel(LconvDev a) {
     store8_bf16(a.ring + rb + static_cast<size_t>((m.pos + 4 + t) & (kConvRing - 1)) * d + e0,
                 win[4 + t]);
   }
+  float w5t[5][8];  // tap-major weights: 2 vector loads per tap
+#pragma unroll
+  for (int k = 0; k < 5; ++k) load8(a.dw + static_cast<size_t>(k) * d + e0, w5t[k]);
   float w5[8][5];
 #pragma unroll
   for (int i = 0; i < 8; ++i)
 #pragma unroll
-    for (int k = 0; k < 5; ++k) w5[i][k] = a.dw[(e0 + i) * 5 + k];
+    for (int k = 0; k < 5; ++k) w5[i][k] = w5t[k][i];
 #pragma unroll
   for (int t = 0; t < 2; ++t) {
     float cv[8];

@@ -62,7 +62,7 @@ struct LayerW {
   float* q_mult;    // [hd] q_scale * softplus(per_dim_scale)
   float* rel_keys;  // [13][d] relative keys, fp32
   float *lc_pre, *lc_norm;
-  float* lc_dw;     // [d][5]
+  float* lc_dw;     // [5][d] tap-major (transposed from [d][1][5] on upload)
   void *w_lstart, *w_lend;
   __half *s_lstart, *s_lend;
   float clip[8][4];  // per linear: in_lo, in_hi, out_lo, out_hi
