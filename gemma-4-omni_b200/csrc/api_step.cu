@@ -74,6 +74,7 @@ bool check_cfg(const lb_config* cfg) {
   const int hd = d / cfg->heads;
   if (hd % 64 || hd > 256 || cfg->heads > 16) return false;
   if (d % 256 || cfg->ffn % 128 || cfg->output_dims % 256 || cfg->text_hidden % 256) return false;
+  if (d > 2048 || d / 256 == 7) return false;  // row kernels are instantiated for d/256 in {1..6, 8}
   if (cfg->sub_ch0 != 128 || cfg->sub_ch1 != 32 || cfg->conv_kernel != 5) return false;
   if (cfg->layers < 1 || cfg->layers > 64) return false;
   if (cfg->weight_format != LB_WEIGHTS_BF16 && cfg->weight_format != LB_WEIGHTS_INT8) return false;

@@ -22,10 +22,11 @@
 //   warp 1      UMMA issuer: tcgen05.mma into one of two TMEM accumulators
 //               (2 x TN fp32 columns), so the epilogue of one unit overlaps the
 //               main loop of the next
-//   warps 2..5  epilogue: tcgen05.ld -> per-channel int8 scale, bias, clamps,
-//               SiLU -> [32 tokens x 128 features] smem staging -> TMA store
-//               (or TMA reduce-add for split-K partial sums)
-//   warps 6..13 int8 only: widen each staged int8 weight tile to bf16 directly
+//   warps 2..9  epilogue, two groups of four warps draining alternate tiles:
+//               tcgen05.ld -> per-channel int8 scale, bias, clamps, SiLU ->
+//               [16 tokens x 128 features] smem staging -> TMA store (or TMA
+//               reduce-add for split-K partial sums)
+//   warps 10..17 int8 only: widen each staged int8 weight tile to bf16 directly
 //               in the 128-byte-swizzled layout UMMA reads (exact: every int8
 //               is a bf16); the scale is applied per accumulator lane.
 // Every wait is bounded (common.cuh); on a timeout the kernel records
@@ -45,44 +46,46 @@ constexpr int kBlockO = 128;
 constexpr int kBlockK = 64;
 constexpr uint32_t kABytes = kBlockO * kBlockK * 2;  // bf16 A tile, 16 KB
 constexpr uint32_t kRawBytes = kBlockO * kBlockK;    // int8 A tile, 8 KB
-constexpr int kChunk = 32;                           // tokens per epilogue chunk
-constexpr uint32_t kStagingBytes = kChunk * kBlockO * 4;  // one fp32 staging buffer, 16 KB
+constexpr int kChunk = 16;                           // tokens per epilogue chunk
+constexpr uint32_t kStagingBytes = kChunk * kBlockO * 4;  // one fp32 staging buffer, 8 KB (x4)
 
 template <int TN, bool WINT8>
 struct GemmCfg {
   static constexpr uint32_t kBBytes = TN * kBlockK * 2;
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
-  // operand ring + 2 staging buffers within 224 KB (the 227 KB opt-in limit
+  // operand ring + 4 staging buffers within 224 KB (the 227 KB opt-in limit
   // leaves room for barriers and the 1 KB alignment slack)
-  static constexpr int kStages = (224 * 1024 - 2 * kStagingBytes) / kStageBytes > 8
+  static constexpr int kStages = (224 * 1024 - 4 * kStagingBytes) / kStageBytes > 8
                                      ? 8
-                                     : (224 * 1024 - 2 * kStagingBytes) / kStageBytes;
+                                     : (224 * 1024 - 4 * kStagingBytes) / kStageBytes;
   static constexpr uint32_t kBarBytes = (4 * kStages + 4) * 8 + 16;
   static constexpr uint32_t kSmemBytes =
-      kStages * kStageBytes + 2 * kStagingBytes + kBarBytes + 1024;
-  static constexpr int kThreads = WINT8 ? 448 : 192;
+      kStages * kStageBytes + 4 * kStagingBytes + kBarBytes + 1024;
+  static constexpr int kThreads = WINT8 ? 576 : 320;
   static constexpr uint32_t kTmemCols = 2 * TN;  // double-buffered accumulator
 };
 
-// Widens 16 int8 to 16 bf16 with full-rate integer/FP ops: flipping the sign
-// bit maps v to u = v + 128 in [0, 255]; placing u in the low mantissa byte of
-// the float 2^23 (bits 0x4B0000uu) gives exactly 2^23 + u, and subtracting
-// 2^23 + 128 recovers v exactly.  |v| <= 128 is exact in bf16.
+// Widens 16 int8 to 16 bf16 with full-rate integer/FP ops only: flipping the
+// sign bit maps v to u = v + 128 in [0, 255]; placing u in the low mantissa
+// byte of the float 2^23 (bits 0x4B0000uu) gives exactly 2^23 + u, and
+// subtracting 2^23 + 128 recovers v exactly as fp32.  A small integer is exact
+// in bf16, so its bf16 bits are the upper half of its fp32 bits: one byte
+// permute packs two of them.
 __device__ __forceinline__ void convert_i8x16_to_bf16(const int4 raw, int4& lo, int4& hi) {
   const uint32_t w[4] = {static_cast<uint32_t>(raw.x) ^ 0x80808080u, static_cast<uint32_t>(raw.y) ^ 0x80808080u,
                          static_cast<uint32_t>(raw.z) ^ 0x80808080u, static_cast<uint32_t>(raw.w) ^ 0x80808080u};
-  __nv_bfloat162 out[8];
+  uint32_t out[8];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const float f0 = __int_as_float(__byte_perm(w[i], 0x4B000000u, 0x7540)) - 8388736.0f;
     const float f1 = __int_as_float(__byte_perm(w[i], 0x4B000000u, 0x7541)) - 8388736.0f;
     const float f2 = __int_as_float(__byte_perm(w[i], 0x4B000000u, 0x7542)) - 8388736.0f;
     const float f3 = __int_as_float(__byte_perm(w[i], 0x4B000000u, 0x7543)) - 8388736.0f;
-    out[2 * i] = __floats2bfloat162_rn(f0, f1);
-    out[2 * i + 1] = __floats2bfloat162_rn(f2, f3);
+    out[2 * i] = __byte_perm(__float_as_uint(f0), __float_as_uint(f1), 0x7632);
+    out[2 * i + 1] = __byte_perm(__float_as_uint(f2), __float_as_uint(f3), 0x7632);
   }
-  lo = *reinterpret_cast<int4*>(&out[0]);
-  hi = *reinterpret_cast<int4*>(&out[4]);
+  lo = make_int4(static_cast<int>(out[0]), static_cast<int>(out[1]), static_cast<int>(out[2]), static_cast<int>(out[3]));
+  hi = make_int4(static_cast<int>(out[4]), static_cast<int>(out[5]), static_cast<int>(out[6]), static_cast<int>(out[7]));
 }
 
 __device__ __forceinline__ void tma_load_2d_nohint(void* dst, const CUtensorMap* map, uint64_t* bar,
@@ -115,7 +118,35 @@ __device__ __forceinline__ void bulk_wait_read1() {
   asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
 }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
-__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// Named barrier of one epilogue group (ids 1 and 2; 0 is __syncthreads).
+__device__ __forceinline__ void epi_bar(int g) {
+  asm volatile("bar.sync %0, 128;" ::"r"(1 + g) : "memory");
+}
+
+// 32 lanes x 16 consecutive fp32 columns per warp.
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// SiLU(x) = x * sigmoid(x) = h + h * tanh(h) with h = x / 2: one hardware
+// tanh (tanh.approx.f32, ~2^-11 relative error) and two FMAs.  The result is
+// rounded to bf16 (2^-8) right after.
+__device__ __forceinline__ float silu_tanh(float x) {
+  const float h = 0.5f * x;
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(h));
+  return fmaf(h, t, h);
+}
 
 struct Unit {
   int o0, t0, kb_begin, nkb, split;
@@ -158,7 +189,7 @@ __global__ void __launch_bounds__(GemmCfg<TN, WINT8>::kThreads, 1)
   // int8 weights land in the upper half of their stage's bf16 A tile
   auto stage_raw = [&](int s) { return smem + s * Cfg::kStageBytes + kRawBytes; };
   uint8_t* staging = smem + S * Cfg::kStageBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(staging + 2 * kStagingBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(staging + 4 * kStagingBytes);
   uint64_t* full = bars;
   uint64_t* empty = bars + S;
   uint64_t* conv = bars + 2 * S;
@@ -255,16 +286,19 @@ __global__ void __launch_bounds__(GemmCfg<TN, WINT8>::kThreads, 1)
         if (ok) umma_commit(&tmem_full[b]);
       }
     }
-  } else if (warp < 6) {
-    // ---------------- epilogue: TMEM -> registers -> smem staging -> TMA store
+  } else if (warp < 10) {
+    // ---------------- epilogue: TMEM -> registers -> smem staging -> TMA store.
+    // Two groups of four warps; group g drains the CTA's units k = g, g+2, ...,
+    // i.e. always accumulator buffer g, so two tiles drain concurrently.
+    const int g = (warp - 2) >> 2;
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const int et = threadIdx.x - 64;
-    const bool leader = et == 0;
-    int local = 0, chunks_issued = 0;
-    for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
+    const bool leader = ((threadIdx.x - 64) & 127) == 0;
+    uint8_t* stg_base = staging + g * 2 * kStagingBytes;
+    int k = g, chunks_issued = 0;
+    for (int u = blockIdx.x + g * gridDim.x; u < units; u += 2 * gridDim.x, k += 2) {
       const Unit w = unit_of(u, o_tiles, t_tiles, TN, p.kb_per_split, total_kb);
-      const int b = local & 1;
-      const uint32_t aph = (local >> 1) & 1;
+      const int b = g;
+      const uint32_t aph = (k >> 1) & 1;
       if (!mbar_wait(&tmem_full[b], aph, p.status)) break;
       tc_fence_after();
       const int o = w.o0 + q * 32 + lane;
@@ -272,33 +306,33 @@ __global__ void __launch_bounds__(GemmCfg<TN, WINT8>::kThreads, 1)
       const float bias = (p.bias && w.split == 0) ? p.bias[o] : 0.0f;
 #pragma unroll 1
       for (int c = 0; c < TN; c += kChunk) {
-        float v[32];
-        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+        float v[kChunk];
+        tmem_ld_32x32b_x16(tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                                static_cast<uint32_t>(b * TN + c), v);
-        if (w.t0 + c >= M) continue;  // uniform across the epilogue warps
-        uint8_t* stg = staging + (chunks_issued & 1) * kStagingBytes;
+        if (w.t0 + c >= M) continue;  // uniform across the group
+        uint8_t* stg = stg_base + (chunks_issued & 1) * kStagingBytes;
         if (leader && chunks_issued >= 2) bulk_wait_read1();  // this buffer's previous store has read smem
-        epi_bar();
+        epi_bar(g);
         if (p.out_mode == 0) {
           __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(stg);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
+          for (int j = 0; j < kChunk; ++j) {
             float y = fminf(fmaxf(fmaf(v[j], scale, bias), p.out_lo), p.out_hi);
-            if (p.act == 1) y = silu_f(bf16_round(y));
+            if (p.act == 1) y = silu_tanh(bf16_round(y));
             y = fminf(fmaxf(y, p.post_lo), p.post_hi);
             st[j * kBlockO + q * 32 + lane] = __float2bfloat16_rn(y);
           }
         } else {
           float* st = reinterpret_cast<float*>(stg);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
+          for (int j = 0; j < kChunk; ++j) {
             float y = fmaf(v[j], scale, bias);
             if (p.out_mode == 1) y = fminf(fmaxf(y, p.out_lo), p.out_hi);
             st[j * kBlockO + q * 32 + lane] = y;
           }
         }
         fence_proxy_async_smem();
-        epi_bar();
+        epi_bar(g);
         if (leader) {
           if (p.out_mode == 2) {
             tma_reduce_add_2d(&tm_out, stg, w.o0, w.t0 + c);
@@ -316,9 +350,9 @@ __global__ void __launch_bounds__(GemmCfg<TN, WINT8>::kThreads, 1)
     }
     if (leader) bulk_wait_all();
   } else {
-    // ---------------- int8 -> bf16 converters (WINT8 only; warps 6..13)
+    // ---------------- int8 -> bf16 converters (WINT8 only; warps 10..17)
     if (WINT8) {
-      const int ct = threadIdx.x - 192;
+      const int ct = threadIdx.x - 320;
       int it = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {

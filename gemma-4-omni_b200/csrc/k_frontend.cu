@@ -139,15 +139,15 @@ __global__ void __launch_bounds__(kSubThreads, 1) subsample_kernel(SubArgs a) {
                                            ~static_cast<uintptr_t>(127));
   __nv_bfloat16* w1s = reinterpret_cast<__nv_bfloat16*>(sp);           // [32][kK1Pad]
   __nv_bfloat16* xin = w1s + 32 * kK1Pad;                              // [5][66][kCiPad]
-  float* w0s = reinterpret_cast<float*>(xin + 5 * 66 * kCiPad);        // [128][9]
-  float* ln0s = w0s + 128 * 9;                                         // [128]
+  float* w0s = reinterpret_cast<float*>(xin + 5 * 66 * kCiPad);        // [128][12] (9 taps + pad)
+  float* ln0s = w0s + 128 * 12;                                        // [128]
   float* mels = ln0s + 128;                                            // [9][130]
   float* c1out = mels + 9 * 130;                                       // [64][33]
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   for (int i = tid; i < 32 * kK1Pad / 8; i += blockDim.x)
     reinterpret_cast<int4*>(w1s)[i] = reinterpret_cast<const int4*>(a.w1)[i];
-  for (int i = tid; i < 128 * 9; i += blockDim.x) w0s[i] = a.w0[i];
+  for (int i = tid; i < 128 * 12; i += blockDim.x) w0s[i] = (i % 12) < 9 ? a.w0[(i / 12) * 9 + i % 12] : 0.f;
   for (int i = tid; i < 128; i += blockDim.x) ln0s[i] = a.ln0[i];
   // zero the frequency padding columns of the conv1 input once (never written)
   for (int i = tid; i < 5 * 2 * kCiPad; i += blockDim.x) {
@@ -191,47 +191,51 @@ __global__ void __launch_bounds__(kSubThreads, 1) subsample_kernel(SubArgs a) {
     __syncthreads();
     // staged mel_prev = last mel row (unmasked)
     for (int i = tid; i < kMelBins; i += blockDim.x) mp_out[i] = mel_in[7 * kMelBins + i];
-    // ---- conv0 + LN(128) + ReLU: warp -> 32 positions, lane -> 4 channels
+    // ---- conv0 + LN(128) + ReLU: thread -> one of the 4 x 64 output positions,
+    // its 3x3 input window in registers; the 9-tap channel outputs are cheap, so
+    // they are recomputed in each of the three passes (mean, centred variance,
+    // output) instead of being held: no cross-thread reduction, no spill.
     __nv_bfloat16* sp_out = a.sub_prev + (static_cast<size_t>(slot) * 2 + (parity ^ 1)) * kF0 * 128;
-    float wr[4][9];
-#pragma unroll
-    for (int cc = 0; cc < 4; ++cc)
-#pragma unroll
-      for (int t = 0; t < 9; ++t) wr[cc][t] = w0s[(lane * 4 + cc) * 9 + t];
-    float g4[4];
-#pragma unroll
-    for (int cc = 0; cc < 4; ++cc) g4[cc] = ln0s[lane * 4 + cc];
-    for (int pi = 0; pi < 32; ++pi) {
-      const int p = warp * 32 + pi;  // 0..255
-      const int t = p >> 6, fq = p & 63;
-      float v[4] = {0.f, 0.f, 0.f, 0.f};
+    {
+      const int t = tid >> 6, fq = tid & 63;
+      float xw[9];
 #pragma unroll
       for (int i = 0; i < 3; ++i)
 #pragma unroll
-        for (int j = 0; j < 3; ++j) {
-          const float xv = mels[(2 * t + i) * 130 + 2 * fq + j];  // padded index = freq + 1
-#pragma unroll
-          for (int cc = 0; cc < 4; ++cc) v[cc] = fmaf(wr[cc][i * 3 + j], xv, v[cc]);
-        }
-      const float mean = warp_sum(v[0] + v[1] + v[2] + v[3]) * (1.0f / 128.0f);
+        for (int j = 0; j < 3; ++j) xw[i * 3 + j] = mels[(2 * t + i) * 130 + 2 * fq + j];  // padded freq + 1
+      auto chan = [&](int c) {
+        const float4 w0 = *reinterpret_cast<const float4*>(w0s + c * 12);
+        const float4 w1 = *reinterpret_cast<const float4*>(w0s + c * 12 + 4);
+        float v = w0.x * xw[0];
+        v = fmaf(w0.y, xw[1], v);
+        v = fmaf(w0.z, xw[2], v);
+        v = fmaf(w0.w, xw[3], v);
+        v = fmaf(w1.x, xw[4], v);
+        v = fmaf(w1.y, xw[5], v);
+        v = fmaf(w1.z, xw[6], v);
+        v = fmaf(w1.w, xw[7], v);
+        return fmaf(w0s[c * 12 + 8], xw[8], v);
+      };
+      float sum = 0.f;
+#pragma unroll 8
+      for (int c = 0; c < 128; ++c) sum += chan(c);
+      const float mean = sum * (1.0f / 128.0f);
       float var = 0.f;
-#pragma unroll
-      for (int cc = 0; cc < 4; ++cc) var += (v[cc] - mean) * (v[cc] - mean);
-      var = warp_sum(var) * (1.0f / 128.0f);
-      const float rstd = rsqrtf(var + a.eps);
-      const float keep = ((mask >> (2 * t)) & 1) ? 1.0f : 0.0f;  // mask0 = mask[::2]
-      __nv_bfloat16 o[4];
-#pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        const float y = fmaxf((v[cc] - mean) * rstd * g4[cc], 0.0f);
-        o[cc] = __float2bfloat16_rn(y);
+#pragma unroll 8
+      for (int c = 0; c < 128; ++c) {
+        const float dv = chan(c) - mean;
+        var = fmaf(dv, dv, var);
       }
-      __nv_bfloat16 om[4];
-#pragma unroll
-      for (int cc = 0; cc < 4; ++cc) om[cc] = __float2bfloat16_rn(__bfloat162float(o[cc]) * keep);
-      *reinterpret_cast<uint2*>(xin + ((1 + t) * 66 + fq + 1) * kCiPad + lane * 4) =
-          *reinterpret_cast<uint2*>(om);
-      if (t == 3) *reinterpret_cast<uint2*>(sp_out + fq * 128 + lane * 4) = *reinterpret_cast<uint2*>(o);
+      const float rstd = rsqrtf(var * (1.0f / 128.0f) + a.eps);
+      const bool keep = (mask >> (2 * t)) & 1;  // mask0 = mask[::2]
+      __nv_bfloat16* xdst = xin + ((1 + t) * 66 + fq + 1) * kCiPad;
+#pragma unroll 4
+      for (int c = 0; c < 128; c += 2) {
+        const __nv_bfloat162 o = __floats2bfloat162_rn(fmaxf((chan(c) - mean) * rstd * ln0s[c], 0.0f),
+                                                       fmaxf((chan(c + 1) - mean) * rstd * ln0s[c + 1], 0.0f));
+        *reinterpret_cast<__nv_bfloat162*>(xdst + c) = keep ? o : __floats2bfloat162_rn(0.f, 0.f);
+        if (t == 3) *reinterpret_cast<__nv_bfloat162*>(sp_out + fq * 128 + c) = o;
+      }
     }
     __syncthreads();
     // ---- conv1 as implicit GEMM on mma.sync: D[pos][co] = sum_k A[pos][k] W1[co][k]
@@ -297,7 +301,7 @@ __global__ void __launch_bounds__(kSubThreads, 1) subsample_kernel(SubArgs a) {
   }
 }
 
-constexpr size_t kSubSmem = 128 + 32 * kK1Pad * 2 + 5 * 66 * kCiPad * 2 + 128 * 9 * 4 + 128 * 4 +
+constexpr size_t kSubSmem = 128 + 32 * kK1Pad * 2 + 5 * 66 * kCiPad * 2 + 128 * 12 * 4 + 128 * 4 +
                             9 * 130 * 4 + 64 * 33 * 4;
 
 }  // namespace

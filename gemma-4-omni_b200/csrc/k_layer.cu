@@ -101,6 +101,7 @@ struct RowFusedDev {
   float* dbg;
 };
 
+// One CTA of d/8 threads per token row, 8 contiguous elements per thread.
 __global__ void __launch_bounds__(256) row_fused_kernel(RowFusedDev a) {
   __shared__ float sh[32];
   const int t = blockIdx.x;
@@ -152,59 +153,75 @@ struct LconvDev {
   float eps, clip, in_lo, in_hi;
 };
 
-__global__ void __launch_bounds__(256) lconv_kernel(LconvDev a) {
-  __shared__ float sh[32];
-  const int row = blockIdx.x;
+// One warp per session (both tick tokens); lane owns G groups of 8 channels,
+// e = (g*32 + lane)*8, so every load is a whole-warp coalesced 512-byte run and
+// the two RMS reductions are warp shuffles.
+template <int G>
+__global__ void __launch_bounds__(128) lconv_kernel(LconvDev a) {
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= a.counts[0]) return;
-  const int d = a.d;
-  const int e0 = threadIdx.x * 8;
+  const int d = G * 256;
   const int slot = a.row_slot[row];
   const SlotMeta m = a.row_meta[row];
   const size_t rb = (static_cast<size_t>(slot) * a.layers + a.layer) * kConvRing * d;
-  float win[6][8];
-  const int first_real = 4 - min(m.fill, 4);
+  const int first_real = 4 - min(m.fill, 4);  // ring rows written since the last reset
+  float cv[2][G][8];
+  float ss0 = 0.f, ss1 = 0.f;
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    if (j >= first_real) {
-      load8_bf16(a.ring + rb + static_cast<size_t>((m.pos + j) & (kConvRing - 1)) * d + e0, win[j]);
-    } else {
+  for (int g = 0; g < G; ++g) {
+    const int e0 = (g * 32 + lane) * 8;
+    float win[6][8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) win[j][i] = 0.f;
+    for (int j = 0; j < 4; ++j) {
+      if (j >= first_real) {
+        load8_bf16(a.ring + rb + static_cast<size_t>((m.pos + j) & (kConvRing - 1)) * d + e0, win[j]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) win[j][i] = 0.f;
+      }
     }
-  }
 #pragma unroll
-  for (int t = 0; t < 2; ++t) {
-    float av[8], bv[8];
-    const __nv_bfloat16* g = a.gl + (static_cast<size_t>(row) * 2 + t) * 2 * d;
-    load8_bf16(g + e0, av);
-    load8_bf16(g + d + e0, bv);
+    for (int t = 0; t < 2; ++t) {
+      float av[8], bv[8];
+      const __nv_bfloat16* gp = a.gl + (static_cast<size_t>(row) * 2 + t) * 2 * d;
+      load8_bf16(gp + e0, av);
+      load8_bf16(gp + d + e0, bv);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) win[4 + t][i] = bf16_round(av[i] / (1.0f + expf(-bv[i])));
-    store8_bf16(a.ring + rb + static_cast<size_t>((m.pos + 4 + t) & (kConvRing - 1)) * d + e0,
-                win[4 + t]);
-  }
-  float w5t[5][8];  // tap-major weights: 2 vector loads per tap
-#pragma unroll
-  for (int k = 0; k < 5; ++k) load8(a.dw + static_cast<size_t>(k) * d + e0, w5t[k]);
-  float w5[8][5];
-#pragma unroll
-  for (int i = 0; i < 8; ++i)
-#pragma unroll
-    for (int k = 0; k < 5; ++k) w5[i][k] = w5t[k][i];
-#pragma unroll
-  for (int t = 0; t < 2; ++t) {
-    float cv[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      float acc = 0.f;
-#pragma unroll
-      for (int k = 0; k < 5; ++k) acc = fmaf(w5[i][k], win[t + k][i], acc);
-      cv[i] = fminf(fmaxf(acc, -a.clip), a.clip);
+      for (int i = 0; i < 8; ++i) win[4 + t][i] = bf16_round(__fdividef(av[i], 1.0f + __expf(-bv[i])));  // GLU
+      store8_bf16(a.ring + rb + static_cast<size_t>((m.pos + 4 + t) & (kConvRing - 1)) * d + e0, win[4 + t]);
     }
-    rms8(cv, a.norm_w, e0, d, a.eps, sh);
+    float w5t[5][8];  // tap-major weights: 2 vector loads per tap
 #pragma unroll
-    for (int i = 0; i < 8; ++i) cv[i] = fminf(fmaxf(silu_f(cv[i]), a.in_lo), a.in_hi);
-    store8_bf16(a.xa + (static_cast<size_t>(row) * 2 + t) * d + e0, cv);
+    for (int k = 0; k < 5; ++k) load8(a.dw + static_cast<size_t>(k) * d + e0, w5t[k]);
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float acc = 0.f;
+#pragma unroll
+        for (int k = 0; k < 5; ++k) acc = fmaf(w5t[k][i], win[t + k][i], acc);
+        acc = fminf(fmaxf(acc, -a.clip), a.clip);
+        cv[t][g][i] = acc;
+        if (t == 0) ss0 = fmaf(acc, acc, ss0);
+        else ss1 = fmaf(acc, acc, ss1);
+      }
+  }
+  const float r0 = rsqrtf(warp_sum(ss0) / static_cast<float>(d) + a.eps);
+  const float r1 = rsqrtf(warp_sum(ss1) / static_cast<float>(d) + a.eps);
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const int e0 = (g * 32 + lane) * 8;
+    float wv[8];
+    load8(a.norm_w + e0, wv);
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      float o[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        o[i] = fminf(fmaxf(silu_f(cv[t][g][i] * (t == 0 ? r0 : r1) * wv[i]), a.in_lo), a.in_hi);
+      store8_bf16(a.xa + (static_cast<size_t>(row) * 2 + t) * d + e0, o);
+    }
   }
 }
 
@@ -358,7 +375,17 @@ cudaError_t launch_lconv(Ctx& c, int layer, int rows_cap, cudaStream_t s) {
   a.clip = c.cfg.gradient_clipping;
   a.in_lo = c.w.layers[layer].clip[7][0];  // linear_end input bounds
   a.in_hi = c.w.layers[layer].clip[7][1];
-  lconv_kernel<<<rows_cap, c.cfg.hidden / 8, 0, s>>>(a);
+  const int grid = (rows_cap + 3) / 4;  // 4 warps (sessions) per CTA
+  switch (c.cfg.hidden / 256) {
+    case 1: lconv_kernel<1><<<grid, 128, 0, s>>>(a); break;
+    case 2: lconv_kernel<2><<<grid, 128, 0, s>>>(a); break;
+    case 3: lconv_kernel<3><<<grid, 128, 0, s>>>(a); break;
+    case 4: lconv_kernel<4><<<grid, 128, 0, s>>>(a); break;
+    case 5: lconv_kernel<5><<<grid, 128, 0, s>>>(a); break;
+    case 6: lconv_kernel<6><<<grid, 128, 0, s>>>(a); break;
+    case 8: lconv_kernel<8><<<grid, 128, 0, s>>>(a); break;
+    default: return cudaErrorInvalidValue;
+  }
   return cudaGetLastError();
 }
 
