@@ -309,7 +309,8 @@ def run_ours(args, pkg, rank, world, device):
 
     # ---- dominant kernel: the int8 FFN1 GEMM at this step's token count, timed alone
     M = 2 * n
-    x = torch.randn(M, FULL.hidden, device=device).to(torch.bfloat16)
+    # int8 weights take fp16 activations, bf16 weights bf16 ones (as inside the step)
+    x = torch.randn(M, FULL.hidden, device=device).to(torch.float16 if fmt == 1 else torch.bfloat16)
     if fmt == 1:
         wq = torch.randint(-127, 128, (FULL.ffn, FULL.hidden), dtype=torch.int8, device=device)
         sc = torch.full((FULL.ffn,), 1e-3, dtype=torch.float16, device=device)

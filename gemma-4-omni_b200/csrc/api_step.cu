@@ -385,7 +385,10 @@ size_t layout_acts(Ctx& c, char* base) {
 int make_op(Ctx& c, GemmOp& op, void* w, const __half* scale, int O, int K, const void* x, int tok_cap,
             const float* bias, void* out, int out_kind, int act, const float* clip4,
             float post_lo = -INFINITY, float post_hi = INFINITY, __nv_bfloat16* final_bf16 = nullptr) {
-  // out_kind: 0 = bf16 (final), 1 = fp32
+  // out_kind: 0 = bf16 tensor, 1 = fp32, 2 = activation that feeds another GEMM
+  // (bf16, or fp16 when the weights are int8)
+  op.final_f16 = out_kind == 2 && c.weight_int8;
+  if (out_kind == 2) out_kind = 0;
   GemmParams& p = op.params;
   p = GemmParams();
   p.m_dev = c.dev_counts + 1;
@@ -417,7 +420,8 @@ int make_op(Ctx& c, GemmOp& op, void* w, const __half* scale, int O, int K, cons
     p.out = out;
   }
   (void)final_bf16;
-  return gemm_prepare(&op.plan, w, c.weight_int8 != 0, O, K, x, K, tok_cap, p.out, O, p.out_mode);
+  return gemm_prepare(&op.plan, w, c.weight_int8 != 0, O, K, x, K, tok_cap, p.out, O, p.out_mode,
+                      op.final_f16);
 }
 
 cudaError_t run_op(Ctx& c, const GemmOp& op, int tok_cap, __nv_bfloat16* final_bf16, cudaStream_t s) {
@@ -432,7 +436,7 @@ cudaError_t run_op(Ctx& c, const GemmOp& op, int tok_cap, __nv_bfloat16* final_b
     // finalize: output clamp -> activation -> next linear's input clamp -> bf16
     float clip4[4] = {op.params.out_lo, op.params.out_hi, op.params.post_lo, op.params.post_hi};
     e = launch_finalize_wide(c, tok_cap, static_cast<const float*>(op.params.out), op.plan.O,
-                             op.params.act, final_bf16, clip4, s);
+                             op.params.act, final_bf16, clip4, op.final_f16, s);
   }
   return e;
 }
@@ -455,7 +459,7 @@ int build_plans(lb_ctx* x, int bi) {
       const float* c2 = L.clip[f == 0 ? kLinFfn1b : kLinFfn2b];
       GemmOp& a1 = f == 0 ? o.ffn1[0] : o.ffn2[0];
       GemmOp& a2 = f == 0 ? o.ffn1[1] : o.ffn2[1];
-      rc |= make_op(c, a1, L.w_ffn1[f], L.s_ffn1[f], F, d, c.xa, tc, nullptr, c.xf, 0, 1, c1, c2[0], c2[1]);
+      rc |= make_op(c, a1, L.w_ffn1[f], L.s_ffn1[f], F, d, c.xa, tc, nullptr, c.xf, 2, 1, c1, c2[0], c2[1]);
       rc |= make_op(c, a2, L.w_ffn2[f], L.s_ffn2[f], d, F, c.xf, tc, nullptr, c.y, 1, 0, c2);
     }
     rc |= make_op(c, o.qkv, L.w_qkv, L.s_qkv, 3 * d, d, c.xa, tc, nullptr, c.qkv, 0, 0, L.clip[kLinQkv]);
@@ -468,7 +472,7 @@ int build_plans(lb_ctx* x, int bi) {
   if (g.film_enabled) {
     const int Q = g.film_query_dim, B = g.film_bottleneck, T = g.text_hidden;
     rc |= make_op(c, P.qdown, c.w.w_qdown, c.w.s_qdown, B, Q, c.film_xq, tc, c.w.b_qdown, c.film_qd, 1, 0, nullptr);
-    rc |= make_op(c, P.rdown, c.w.w_rdown, c.w.s_rdown, B, T, c.film_xr, tc, c.w.b_rdown, c.film_rd_bf, 0, 1, nullptr);
+    rc |= make_op(c, P.rdown, c.w.w_rdown, c.w.s_rdown, B, T, c.film_xr, tc, c.w.b_rdown, c.film_rd_bf, 2, 1, nullptr);
     rc |= make_op(c, P.film, c.w.w_film, c.w.s_film, 2 * B, B, c.film_rd_bf, tc, c.w.b_film, c.film_gb, 1, 0, nullptr);
     rc |= make_op(c, P.fout, c.w.w_fout, c.w.s_fout, Q, B, c.film_fused, tc, c.w.b_fout, c.film_map, 1, 0, nullptr);
   }

@@ -196,13 +196,49 @@ __device__ __forceinline__ uint64_t smem_desc_k128(uint32_t smem_addr) {
   return d;
 }
 
-// Instruction descriptor for kind::f16: bf16 A/B, f32 D, both K-major.
+// Instruction descriptor for kind::f16: bf16 (or fp16) A/B, f32 D, both K-major.
 __host__ __device__ constexpr uint32_t umma_idesc_bf16(int m, int n) {
   return (1u << 4)                                  // D format f32
          | (1u << 7)                                // A bf16
          | (1u << 10)                               // B bf16
          | (static_cast<uint32_t>(n >> 3) << 17)    // N / 8
          | (static_cast<uint32_t>(m >> 4) << 24);   // M / 16
+}
+__host__ __device__ constexpr uint32_t umma_idesc_f16(int m, int n) {
+  return (1u << 4)                                  // D format f32; A, B format 0 = f16
+         | (static_cast<uint32_t>(n >> 3) << 17)
+         | (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+// ------------------------------------------ GEMM-input activation stores
+// Activations that feed a GEMM are bf16, or fp16 when the weights are int8
+// (int8 widens to fp16 in two integer ops; fp16 keeps 3 more mantissa bits).
+// fp16 stores saturate at +/-65504 instead of overflowing to infinity.
+constexpr float kF16Max = 65504.0f;
+__device__ __forceinline__ uint16_t act_bits(float v, bool f16) {
+  if (f16) return __half_as_ushort(__float2half_rn(fminf(fmaxf(v, -kF16Max), kF16Max)));
+  return __bfloat16_as_ushort(__float2bfloat16_rn(v));
+}
+__device__ __forceinline__ uint32_t act_bits2(float a, float b, bool f16) {
+  if (f16) {
+    const __half2 h = __floats2half2_rn(fminf(fmaxf(a, -kF16Max), kF16Max), fminf(fmaxf(b, -kF16Max), kF16Max));
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+// 8 consecutive activations (16-byte store)
+__device__ __forceinline__ void store8_act(void* p, const float (&v)[8], bool f16) {
+  int4 r;
+  r.x = static_cast<int>(act_bits2(v[0], v[1], f16));
+  r.y = static_cast<int>(act_bits2(v[2], v[3], f16));
+  r.z = static_cast<int>(act_bits2(v[4], v[5], f16));
+  r.w = static_cast<int>(act_bits2(v[6], v[7], f16));
+  *reinterpret_cast<int4*>(p) = r;
+}
+__device__ __forceinline__ float act_load(const void* p, bool f16) {
+  const uint16_t b = *reinterpret_cast<const uint16_t*>(p);
+  return f16 ? __half2float(__ushort_as_half(b)) : __bfloat162float(__ushort_as_bfloat16(b));
 }
 
 // ------------------------------------------------------------ misc math

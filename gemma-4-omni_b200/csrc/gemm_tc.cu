@@ -65,24 +65,23 @@ struct GemmCfg {
   static constexpr uint32_t kTmemCols = 2 * TN;  // double-buffered accumulator
 };
 
-// Widens 16 int8 to 16 bf16 with full-rate integer/FP ops only: flipping the
-// sign bit maps v to u = v + 128 in [0, 255]; placing u in the low mantissa
-// byte of the float 2^23 (bits 0x4B0000uu) gives exactly 2^23 + u, and
-// subtracting 2^23 + 128 recovers v exactly as fp32.  A small integer is exact
-// in bf16, so its bf16 bits are the upper half of its fp32 bits: one byte
-// permute packs two of them.
-__device__ __forceinline__ void convert_i8x16_to_bf16(const int4 raw, int4& lo, int4& hi) {
+// Widens 16 int8 to 16 fp16 with two byte permutes and two packed fp16
+// subtractions per four values: flipping the sign bit maps v to u = v + 128 in
+// [0, 255]; the fp16 bit pattern 0x6400 | u is exactly 1024 + u, so
+// subtracting 1152 recovers v exactly (every |v| <= 128 is exact in fp16).
+__device__ __forceinline__ void convert_i8x16_to_f16(const int4 raw, int4& lo, int4& hi) {
   const uint32_t w[4] = {static_cast<uint32_t>(raw.x) ^ 0x80808080u, static_cast<uint32_t>(raw.y) ^ 0x80808080u,
                          static_cast<uint32_t>(raw.z) ^ 0x80808080u, static_cast<uint32_t>(raw.w) ^ 0x80808080u};
+  const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));  // 1152
   uint32_t out[8];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const float f0 = __int_as_float(__byte_perm(w[i], 0x4B000000u, 0x7540)) - 8388736.0f;
-    const float f1 = __int_as_float(__byte_perm(w[i], 0x4B000000u, 0x7541)) - 8388736.0f;
-    const float f2 = __int_as_float(__byte_perm(w[i], 0x4B000000u, 0x7542)) - 8388736.0f;
-    const float f3 = __int_as_float(__byte_perm(w[i], 0x4B000000u, 0x7543)) - 8388736.0f;
-    out[2 * i] = __byte_perm(__float_as_uint(f0), __float_as_uint(f1), 0x7632);
-    out[2 * i + 1] = __byte_perm(__float_as_uint(f2), __float_as_uint(f3), 0x7632);
+    uint32_t p0 = __byte_perm(w[i], 0x64646464u, 0x5140);  // {0x64|u0, 0x64|u1}
+    uint32_t p1 = __byte_perm(w[i], 0x64646464u, 0x5342);  // {0x64|u2, 0x64|u3}
+    __half2 h0 = __hsub2(*reinterpret_cast<__half2*>(&p0), bias);
+    __half2 h1 = __hsub2(*reinterpret_cast<__half2*>(&p1), bias);
+    out[2 * i] = *reinterpret_cast<uint32_t*>(&h0);
+    out[2 * i + 1] = *reinterpret_cast<uint32_t*>(&h1);
   }
   lo = make_int4(static_cast<int>(out[0]), static_cast<int>(out[1]), static_cast<int>(out[2]), static_cast<int>(out[3]));
   hi = make_int4(static_cast<int>(out[4]), static_cast<int>(out[5]), static_cast<int>(out[6]), static_cast<int>(out[7]));
@@ -256,7 +255,8 @@ __global__ void __launch_bounds__(GemmCfg<TN, WINT8>::kThreads, 1)
   } else if (warp == 1) {
     // ---------------- UMMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_bf16(kBlockO, TN);
+      // int8 weights run with fp16 operands (widened W, fp16 activations)
+      constexpr uint32_t idesc = WINT8 ? umma_idesc_f16(kBlockO, TN) : umma_idesc_bf16(kBlockO, TN);
       int it = 0, local = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++local) {
@@ -314,13 +314,14 @@ __global__ void __launch_bounds__(GemmCfg<TN, WINT8>::kThreads, 1)
         if (leader && chunks_issued >= 2) bulk_wait_read1();  // this buffer's previous store has read smem
         epi_bar(g);
         if (p.out_mode == 0) {
-          __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(stg);
+          uint16_t* st = reinterpret_cast<uint16_t*>(stg);
+          const bool f16 = p.out_f16 != 0;
 #pragma unroll
           for (int j = 0; j < kChunk; ++j) {
             float y = fminf(fmaxf(fmaf(v[j], scale, bias), p.out_lo), p.out_hi);
             if (p.act == 1) y = silu_tanh(bf16_round(y));
             y = fminf(fmaxf(y, p.post_lo), p.post_hi);
-            st[j * kBlockO + q * 32 + lane] = __float2bfloat16_rn(y);
+            st[j * kBlockO + q * 32 + lane] = act_bits(y, f16);
           }
         } else {
           float* st = reinterpret_cast<float*>(stg);
@@ -386,7 +387,7 @@ __global__ void __launch_bounds__(GemmCfg<TN, WINT8>::kThreads, 1)
             const int row = cidx >> 2;
             const int ch = cidx & 3;
             int4 lo, hi;
-            convert_i8x16_to_bf16(r[qd], lo, hi);
+            convert_i8x16_to_f16(r[qd], lo, hi);
             const int sw = row & 7;
             *reinterpret_cast<int4*>(dst + row * 128 + (((2 * ch) ^ sw) << 4)) = lo;
             *reinterpret_cast<int4*>(dst + row * 128 + (((2 * ch + 1) ^ sw) << 4)) = hi;
@@ -464,10 +465,11 @@ cudaError_t gemm_init_attributes() {
 
 int make_tensor_map_2d(CUtensorMap* map, const void* base, int elem_bytes, uint64_t inner,
                        uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
-                       uint32_t box_outer, bool swizzle128) {
+                       uint32_t box_outer, bool swizzle128, bool f16) {
   auto enc = tensor_map_encoder();
   if (!enc) return -1;
-  const CUtensorMapDataType dt = elem_bytes == 2   ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+  const CUtensorMapDataType dt = elem_bytes == 2   ? (f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                          : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16)
                                  : elem_bytes == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                                    : CU_TENSOR_MAP_DATA_TYPE_UINT8;
   cuuint64_t dims[2] = {inner, outer};
@@ -489,7 +491,7 @@ int gemm_token_tile(int m_cap) {
 }
 
 int gemm_prepare(GemmPlan* plan, const void* w, bool w_int8, int O, int K, const void* x, int x_ld,
-                 int m_cap, void* out, int ld_out, int out_mode) {
+                 int m_cap, void* out, int ld_out, int out_mode, bool out_f16) {
   if (O % kBlockO != 0 || K % kBlockK != 0 || x_ld % 8 != 0 || ld_out % 8 != 0 || m_cap < 1)
     return -3;
   plan->O = O;
@@ -498,6 +500,7 @@ int gemm_prepare(GemmPlan* plan, const void* w, bool w_int8, int O, int K, const
   plan->m_cap = m_cap;
   plan->tn = gemm_token_tile(m_cap);
   plan->out_mode = out_mode;
+  plan->out_f16 = out_f16;
   int rc;
   if (w_int8) {
     rc = make_tensor_map_2d(&plan->tm_w, w, 1, K, O, static_cast<uint64_t>(K), kBlockK, kBlockO,
@@ -513,24 +516,27 @@ int gemm_prepare(GemmPlan* plan, const void* w, bool w_int8, int O, int K, const
   // then hold stale data that only reaches output columns t >= m_cap, which are
   // clipped by the output map.
   plan->x_box_rows = m_cap < plan->tn ? m_cap : plan->tn;
+  // activations are fp16 when the weights are int8, bf16 otherwise
   rc = make_tensor_map_2d(&plan->tm_x, x, 2, K, static_cast<uint64_t>(m_cap),
                           static_cast<uint64_t>(x_ld) * 2, kBlockK,
-                          static_cast<uint32_t>(plan->x_box_rows), true);
+                          static_cast<uint32_t>(plan->x_box_rows), true, w_int8);
   if (rc) return rc;
-  // Output map: [m_cap rows][ld_out], stores of 32-token x 128-feature boxes.
+  // Output map: [m_cap rows][ld_out], stores of 16-token x 128-feature boxes.
   // Rows t >= m_cap are clipped by TMA; rows in [M, m_cap) receive values of
   // columns the kernel computed from stale activation rows -- never read.
   const int ebytes = out_mode == 0 ? 2 : 4;
   plan->out_box_rows = m_cap < kChunk ? m_cap : kChunk;
   return make_tensor_map_2d(&plan->tm_out, out, ebytes, static_cast<uint64_t>(O),
                             static_cast<uint64_t>(m_cap), static_cast<uint64_t>(ld_out) * ebytes,
-                            kBlockO, static_cast<uint32_t>(plan->out_box_rows), false);
+                            kBlockO, static_cast<uint32_t>(plan->out_box_rows), false,
+                            out_mode == 0 && out_f16);
 }
 
 cudaError_t gemm_launch(const GemmPlan& plan, GemmParams p, int splits, cudaStream_t stream) {
   p.O = plan.O;
   p.K = plan.K;
   p.b_tx_bytes = static_cast<uint32_t>(plan.x_box_rows) * kBlockK * 2;
+  p.out_f16 = plan.out_f16 ? 1 : 0;
   if (p.out_mode != plan.out_mode) return cudaErrorInvalidValue;
   const int total_kb = plan.K / kBlockK;
   if (splits < 1) splits = 1;

@@ -41,6 +41,7 @@ struct AttnDev {
   int layer, layers, d;
   float k_scale, softcap, invalid;
   float in_lo, in_hi;  // attention.post input clamp
+  bool f16;            // out holds fp16 (int8-weight GEMM input) instead of bf16
 };
 
 template <int HD>
@@ -182,10 +183,10 @@ __global__ void __launch_bounds__(512) attention_kernel(AttnDev a) {
 #pragma unroll
   for (int r = 0; r < NP; ++r) {
     const int e = 2 * lane + 64 * r;
-    *reinterpret_cast<__nv_bfloat162*>(dst0 + e) =
-        __floats2bfloat162_rn(fminf(fmaxf(o0[2 * r], a.in_lo), a.in_hi), fminf(fmaxf(o0[2 * r + 1], a.in_lo), a.in_hi));
-    *reinterpret_cast<__nv_bfloat162*>(dst0 + d + e) =
-        __floats2bfloat162_rn(fminf(fmaxf(o1[2 * r], a.in_lo), a.in_hi), fminf(fmaxf(o1[2 * r + 1], a.in_lo), a.in_hi));
+    *reinterpret_cast<uint32_t*>(dst0 + e) =
+        act_bits2(fminf(fmaxf(o0[2 * r], a.in_lo), a.in_hi), fminf(fmaxf(o0[2 * r + 1], a.in_lo), a.in_hi), a.f16);
+    *reinterpret_cast<uint32_t*>(dst0 + d + e) =
+        act_bits2(fminf(fmaxf(o1[2 * r], a.in_lo), a.in_hi), fminf(fmaxf(o1[2 * r + 1], a.in_lo), a.in_hi), a.f16);
   }
   // ---- stage the two new K/V entries at ring positions pos+13, pos+14
 #pragma unroll
@@ -238,6 +239,7 @@ cudaError_t launch_attention(Ctx& c, int layer, int rows_cap, cudaStream_t s) {
   a.invalid = c.cfg.invalid_logit;
   a.in_lo = c.w.layers[layer].clip[5][0];
   a.in_hi = c.w.layers[layer].clip[5][1];
+  a.f16 = c.weight_int8 != 0;
   const int threads = 32 * c.cfg.heads;
   const size_t smem = attention_smem_bytes(c.cfg.heads);
   switch (c.hd) {

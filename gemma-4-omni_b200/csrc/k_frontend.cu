@@ -121,6 +121,7 @@ struct SubArgs {
   __nv_bfloat16* sub_in;        // [tok][32 * C1]  index f * C1 + c
   float eps;
   int c1;                       // conv1 output channels (32)
+  bool f16;                     // sub_in holds fp16 (int8-weight GEMM input) instead of bf16
 };
 
 __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
@@ -295,7 +296,7 @@ __global__ void __launch_bounds__(kSubThreads, 1) subsample_kernel(SubArgs a) {
       for (int c = 0; c < 32; c += 2) {
         const float y0 = fmaxf((c1out[p * 33 + c] - mean) * rstd * a.ln1[c], 0.f);
         const float y1 = fmaxf((c1out[p * 33 + c + 1] - mean) * rstd * a.ln1[c + 1], 0.f);
-        *reinterpret_cast<__nv_bfloat162*>(o + c) = __floats2bfloat162_rn(y0, y1);
+        *reinterpret_cast<uint32_t*>(o + c) = act_bits2(y0, y1, a.f16);
       }
     }
   }
@@ -344,6 +345,7 @@ cudaError_t launch_subsample(Ctx& c, int rows_cap, cudaStream_t s) {
   a.w1 = c.w.conv1;
   a.ln1 = c.w.ln1;
   a.sub_in = c.sub_in;
+  a.f16 = c.weight_int8 != 0;
   a.eps = c.cfg.rms_eps;
   a.c1 = c.cfg.sub_ch1;
   int grid = rows_cap < c.num_sms ? rows_cap : c.num_sms;

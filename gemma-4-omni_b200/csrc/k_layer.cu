@@ -99,6 +99,7 @@ struct RowFusedDev {
   float in_lo, in_hi;
   __nv_bfloat16* xa;
   float* dbg;
+  bool f16;  // xa holds fp16 (int8-weight GEMM input) instead of bf16
 };
 
 // One CTA of d/8 threads per token row, 8 contiguous elements per thread.
@@ -135,7 +136,7 @@ __global__ void __launch_bounds__(256) row_fused_kernel(RowFusedDev a) {
     if (a.pre_norm) rms8(xv, a.pre_w, e0, a.d, a.eps, sh);
 #pragma unroll
     for (int i = 0; i < 8; ++i) xv[i] = fminf(fmaxf(xv[i], a.in_lo), a.in_hi);
-    store8_bf16(a.xa + base, xv);
+    store8_act(a.xa + base, xv, a.f16);
   }
 }
 
@@ -151,6 +152,7 @@ struct LconvDev {
   __nv_bfloat16* xa;         // [tok][d]
   int layer, layers, d;
   float eps, clip, in_lo, in_hi;
+  bool f16;  // xa holds fp16 (int8-weight GEMM input) instead of bf16
 };
 
 // One warp per session (both tick tokens); lane owns G groups of 8 channels,
@@ -220,14 +222,15 @@ __global__ void __launch_bounds__(128) lconv_kernel(LconvDev a) {
 #pragma unroll
       for (int i = 0; i < 8; ++i)
         o[i] = fminf(fmaxf(silu_f(cv[t][g][i] * (t == 0 ? r0 : r1) * wv[i]), a.in_lo), a.in_hi);
-      store8_bf16(a.xa + (static_cast<size_t>(row) * 2 + t) * d + e0, o);
+      store8_act(a.xa + (static_cast<size_t>(row) * 2 + t) * d + e0, o, a.f16);
     }
   }
 }
 
 // ------------------------------------------------------- split-K finalize
 __global__ void finalize_wide_kernel(const int* counts, const float* acc, int width, int act,
-                                     __nv_bfloat16* out, float lo, float hi, float plo, float phi) {
+                                     __nv_bfloat16* out, float lo, float hi, float plo, float phi,
+                                     bool f16) {
   const int t = blockIdx.y;
   if (t >= counts[1]) return;
   const int o = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
@@ -240,7 +243,7 @@ __global__ void finalize_wide_kernel(const int* counts, const float* acc, int wi
     if (act == 1) y = silu_f(bf16_round(y));
     v[i] = fminf(fmaxf(y, plo), phi);
   }
-  store8_bf16(out + static_cast<size_t>(t) * width + o, v);
+  store8_act(out + static_cast<size_t>(t) * width + o, v, f16);
 }
 
 // ----------------------------------------------------------- output tails
@@ -248,7 +251,7 @@ __global__ void finalize_wide_kernel(const int* counts, const float* acc, int wi
 // stage 1: y = embed(...) fp32 -> soft bf16
 __global__ void __launch_bounds__(256) outputs_kernel(const int* counts, const float* y, int width,
                                                      int stage, __nv_bfloat16* out,
-                                                     __nv_bfloat16* next_in, float eps) {
+                                                     __nv_bfloat16* next_in, float eps, bool f16) {
   __shared__ float sh[32];
   const int t = blockIdx.x;
   if (t >= counts[1]) return;
@@ -260,7 +263,7 @@ __global__ void __launch_bounds__(256) outputs_kernel(const int* counts, const f
   store8_bf16(out + static_cast<size_t>(t) * width + e0, v);
   if (stage == 0) {
     rms8(v, nullptr, e0, width, eps, sh);
-    store8_bf16(next_in + static_cast<size_t>(t) * width + e0, v);
+    store8_act(next_in + static_cast<size_t>(t) * width + e0, v, f16);
   }
 }
 
@@ -270,7 +273,7 @@ __global__ void __launch_bounds__(256) film_norm_kernel(const int* counts, const
                                                        const float* qw, const float* qb,
                                                        const float* hw, const float* hb,
                                                        __nv_bfloat16* xq, __nv_bfloat16* xr,
-                                                       float* amp) {
+                                                       float* amp, bool f16) {
   __shared__ float sh[32];
   const int t = blockIdx.x;
   if (t >= counts[1]) return;
@@ -303,21 +306,21 @@ __global__ void __launch_bounds__(256) film_norm_kernel(const int* counts, const
       load8(b + e, bv);
 #pragma unroll
       for (int i = 0; i < 8; ++i) v[i] = (v[i] - mean) * rstd * wv[i] + bv[i];
-      store8_bf16(dst + e, v);
+      store8_act(dst + e, v, f16);
     }
   }
 }
 
 // FiLM stage 1: fused = SiLU(qd * (1 + tanh(gamma)) + beta) -> bf16
 __global__ void film_fuse_kernel(const int* counts, const float* qd, const float* gb, int bdim,
-                                 __nv_bfloat16* fused) {
+                                 __nv_bfloat16* fused, bool f16) {
   const int t = blockIdx.x;
   if (t >= counts[1]) return;
   for (int e = threadIdx.x; e < bdim; e += blockDim.x) {
     const float g = gb[static_cast<size_t>(t) * 2 * bdim + e];
     const float b = gb[static_cast<size_t>(t) * 2 * bdim + bdim + e];
     const float v = qd[static_cast<size_t>(t) * bdim + e] * (1.0f + tanhf(g)) + b;
-    fused[static_cast<size_t>(t) * bdim + e] = __float2bfloat16_rn(silu_f(v));
+    reinterpret_cast<uint16_t*>(fused)[static_cast<size_t>(t) * bdim + e] = act_bits(silu_f(v), f16);
   }
 }
 
@@ -354,6 +357,7 @@ cudaError_t launch_row_fused(Ctx& c, int tok_cap, const RowFusedArgs& r, cudaStr
   a.in_hi = r.in_hi;
   a.xa = r.xa;
   a.dbg = r.dbg;
+  a.f16 = c.weight_int8 != 0;
   row_fused_kernel<<<tok_cap, c.cfg.hidden / 8, 0, s>>>(a);
   return cudaGetLastError();
 }
@@ -375,6 +379,7 @@ cudaError_t launch_lconv(Ctx& c, int layer, int rows_cap, cudaStream_t s) {
   a.clip = c.cfg.gradient_clipping;
   a.in_lo = c.w.layers[layer].clip[7][0];  // linear_end input bounds
   a.in_hi = c.w.layers[layer].clip[7][1];
+  a.f16 = c.weight_int8 != 0;
   const int grid = (rows_cap + 3) / 4;  // 4 warps (sessions) per CTA
   switch (c.cfg.hidden / 256) {
     case 1: lconv_kernel<1><<<grid, 128, 0, s>>>(a); break;
@@ -390,14 +395,15 @@ cudaError_t launch_lconv(Ctx& c, int layer, int rows_cap, cudaStream_t s) {
 }
 
 cudaError_t launch_finalize_wide(Ctx& c, int tok_cap, const float* acc, int width, int act,
-                                 __nv_bfloat16* out, const float* out_clip, cudaStream_t s) {
+                                 __nv_bfloat16* out, const float* out_clip, bool out_f16,
+                                 cudaStream_t s) {
   const int per_block = 128 * 8;
   dim3 grid((width + per_block - 1) / per_block, tok_cap);
   finalize_wide_kernel<<<grid, 128, 0, s>>>(c.dev_counts, acc, width, act, out,
                                             out_clip ? out_clip[0] : -INFINITY,
                                             out_clip ? out_clip[1] : INFINITY,
                                             out_clip ? out_clip[2] : -INFINITY,
-                                            out_clip ? out_clip[3] : INFINITY);
+                                            out_clip ? out_clip[3] : INFINITY, out_f16);
   return cudaGetLastError();
 }
 
@@ -405,7 +411,7 @@ cudaError_t launch_outputs(Ctx& c, int tok_cap, int stage, cudaStream_t s) {
   const int width = stage == 0 ? c.cfg.output_dims : c.cfg.text_hidden;
   outputs_kernel<<<tok_cap, width / 8, 0, s>>>(c.dev_counts, c.y, width, stage,
                                                stage == 0 ? c.out_raw : c.out_soft, c.xe,
-                                               c.cfg.rms_eps);
+                                               c.cfg.rms_eps, c.weight_int8 != 0);
   return cudaGetLastError();
 }
 
@@ -414,9 +420,11 @@ cudaError_t launch_film(Ctx& c, int tok_cap, int stage, cudaStream_t s) {
   if (stage == 0) {
     film_norm_kernel<<<tok_cap, 128, 0, s>>>(c.dev_counts, c.in_query, Q, c.out_soft, T,
                                              c.w.fq_norm_w, c.w.fq_norm_b, c.w.fr_norm_w,
-                                             c.w.fr_norm_b, c.film_xq, c.film_xr, c.film_amp);
+                                             c.w.fr_norm_b, c.film_xq, c.film_xr, c.film_amp,
+                                             c.weight_int8 != 0);
   } else if (stage == 1) {
-    film_fuse_kernel<<<tok_cap, 128, 0, s>>>(c.dev_counts, c.film_qd, c.film_gb, B, c.film_fused);
+    film_fuse_kernel<<<tok_cap, 128, 0, s>>>(c.dev_counts, c.film_qd, c.film_gb, B, c.film_fused,
+                                             c.weight_int8 != 0);
   } else {
     dim3 grid((Q + 255) / 256, tok_cap);
     film_out_kernel<<<grid, 256, 0, s>>>(c.dev_counts, c.film_map, c.in_query, c.film_amp, Q,

@@ -29,6 +29,7 @@ struct GemmParams {
   float post_lo = -INFINITY, post_hi = INFINITY;  // next linear's input clamp (after act)
   int* status = nullptr;
   uint32_t b_tx_bytes = 0;  // bytes one activation-tile TMA load delivers (set by gemm_launch)
+  int out_f16 = 0;          // out_mode 0 stores fp16 instead of bf16 (set by gemm_launch)
 };
 
 struct GemmPlan {
@@ -39,18 +40,20 @@ struct GemmPlan {
   int x_box_rows = 0;    // rows per activation TMA box: min(tn, m_cap)
   int out_box_rows = 0;  // rows per output TMA box: min(32, m_cap)
   int out_mode = 0;
+  bool out_f16 = false;
   bool w_int8 = false;
 };
 
 int make_tensor_map_2d(CUtensorMap* map, const void* base, int elem_bytes, uint64_t inner,
                        uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
-                       uint32_t box_outer, bool swizzle128);
+                       uint32_t box_outer, bool swizzle128, bool f16 = false);
 int gemm_token_tile(int m_cap);
 // Encodes the tensor maps for W ([O,K] bf16 or int8), X ([m_cap,K], row stride
-// x_ld elements; TMA zero-fills rows past m_cap) and the output ([m_cap, ld_out],
-// bf16 for out_mode 0, fp32 otherwise; stores past m_cap are clipped).
+// x_ld elements; bf16, or fp16 when W is int8; TMA zero-fills rows past m_cap)
+// and the output ([m_cap, ld_out]: out_mode 0 bf16 or, with out_f16, fp16;
+// fp32 otherwise; stores past m_cap are clipped).
 int gemm_prepare(GemmPlan* plan, const void* w, bool w_int8, int O, int K, const void* x, int x_ld,
-                 int m_cap, void* out, int ld_out, int out_mode);
+                 int m_cap, void* out, int ld_out, int out_mode, bool out_f16 = false);
 cudaError_t gemm_launch(const GemmPlan& plan, GemmParams p, int splits, cudaStream_t stream);
 // K-split count that fills the SMs for an [m_cap x O] output with K reduction.
 int gemm_pick_splits(int O, int K, int m_cap, int num_sms);

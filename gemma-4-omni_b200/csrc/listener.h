@@ -106,6 +106,7 @@ struct GemmOp {
   GemmPlan plan;
   GemmParams params;
   int splits = 1;
+  bool final_f16 = false;  // output feeds another GEMM in fp16 (int8 weights)
 };
 
 struct Bucket {
@@ -230,7 +231,7 @@ cudaError_t launch_row_fused(Ctx& c, int tok_cap, const RowFusedArgs& a, cudaStr
 cudaError_t launch_attention(Ctx& c, int layer, int rows_cap, cudaStream_t s);
 cudaError_t launch_lconv(Ctx& c, int layer, int rows_cap, cudaStream_t s);
 cudaError_t launch_finalize_wide(Ctx& c, int tok_cap, const float* acc, int width, int act,
-                                 __nv_bfloat16* out, const float* out_clip, cudaStream_t s);
+                                 __nv_bfloat16* out, const float* out_clip, bool out_f16, cudaStream_t s);
 cudaError_t launch_outputs(Ctx& c, int tok_cap, int stage, cudaStream_t s);
 cudaError_t launch_film(Ctx& c, int tok_cap, int stage, cudaStream_t s);
 

@@ -180,7 +180,8 @@ int lb_debug_set_expected(lb_ctx* ctx, int32_t handle, int64_t frame, int64_t se
 /* Diagnostics: make the next lb_step_async run eagerly and stop after stage
  * `stage` (0..12) of layer `layer` (-1 disables); lb_debug_read_buffer copies
  * an internal activation ("h", "y", "xa", "xf", "qkv", "att", "gl", "mel",
- * "sub_in") to host memory (synchronous). */
+ * "sub_in") to host memory (synchronous).  GEMM-input buffers ("xa", "xf",
+ * "att", "sub_in") hold fp16 instead of bf16 when the weights are int8. */
 int lb_debug_set_stop(lb_ctx* ctx, int layer, int stage);
 int lb_debug_read_buffer(lb_ctx* ctx, const char* name, void* host_dst, size_t bytes, void* stream);
 
@@ -191,8 +192,10 @@ int lb_debug_read_buffer(lb_ctx* ctx, const char* name, void* host_dst, size_t b
 /* D[t,o] = sum_k X[t,k] W[o,k] (+bias[o]) on tcgen05 tensor cores.
  * Replaces Gemma4ClippableLinear.forward / the reference Triton clipped
  * linear (duplex_kernel/streaming_conformer_kernels.py:27-76, 110-168).
- * x: bf16 [m, x_ld] (K-contiguous, x_ld % 8 == 0); w: bf16 [out_features, k]
- * or int8 with w_scale fp16 [out_features]; out_mode 0 = bf16, 1 = fp32,
+ * w: bf16 [out_features, k], or int8 with w_scale fp16 [out_features];
+ * x: [m, x_ld] (K-contiguous, x_ld % 8 == 0), bf16 with bf16 weights and
+ * fp16 with int8 weights (the int8 codes widen exactly to fp16 and the
+ * product runs as an fp16 x fp16 MMA); out_mode 0 = bf16, 1 = fp32,
  * 2 = fp32 atomic accumulate (caller zeroes out; required when splits > 1);
  * act 1 = SiLU of the bf16-rounded product (bf16 output only).
  * out_features % 128 == 0, k % 64 == 0. */

@@ -16,7 +16,8 @@ def lib(pkg):
 def run_gemm(lib, M, O, K, int8, mode, act, splits, bias, seed):
     g = torch.Generator().manual_seed(seed)
     dev = torch.device("cuda")
-    x = (torch.randn(M, K, generator=g) * 0.5).to(torch.bfloat16).to(dev)
+    # int8 weights take fp16 activations (the int8 codes widen exactly to fp16)
+    x = (torch.randn(M, K, generator=g) * 0.5).to(torch.float16 if int8 else torch.bfloat16).to(dev)
     if int8:
         wq = torch.randint(-127, 128, (O, K), generator=g, dtype=torch.int8).to(dev)
         sc = (torch.rand(O, generator=g) * 1e-3 + 1e-4).to(torch.float16).to(dev)
