@@ -203,6 +203,22 @@ int lb_op_gemm(const void* x, int x_ld, int m, const void* w, int w_int8, const 
                const float* bias, int out_features, int k, void* out, int ld_out, int out_mode,
                int act, int splits, int* status_dev, void* stream);
 
+/* lb_op_gemm's split-K form with a bf16 output [m, ld_out] and no
+ * caller-supplied accumulator: the fp32 partial sums of the `splits` K slices
+ * are reduce-added into a fixed device array inside the library (8 MiB, i.e.
+ * m * out_features <= 2097152 fp32 values; larger sizes return
+ * LB_ERR_CAPACITY), then rounded to bf16 (act 1: SiLU of the bf16-rounded sum).
+ * Nothing is allocated by any call.  The first call on a device (that device
+ * current) resolves the array's address and sets the GEMM kernel attributes,
+ * so make it before any stream capture.  There is one array per device:
+ * calls that overlap on the GPU race.  x / w / w_scale / bias as lb_op_gemm.
+ * No counterpart in the reference: it exists for callers that must not
+ * allocate device memory per call. */
+int lb_op_gemm_splitk_scratch(const void* x, int x_ld, int m, const void* w, int w_int8,
+                              const void* w_scale, const float* bias, int out_features, int k,
+                              void* out, int ld_out, int act, int splits, int* status_dev,
+                              void* stream);
+
 #ifdef __cplusplus
 }
 #endif
