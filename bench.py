@@ -428,6 +428,12 @@ def main():
     M = res["M"]
     gemm_flops = 2.0 * M * FULL.ffn * FULL.hidden
     achieved = gemm_flops / (res["gemm_ms"] * 1e-3) / 1e12
+    # DRAM bytes (read + write) of one launch of this GEMM from an ncu --set full
+    # capture of the same shape (M=2048, int8 weights, fp16 activations): W and X
+    # are read once (15.79 MB); the 25 MB output stays in L2 by kernel end.
+    traffic, traffic_src = None, None
+    if M == 2048 and args.weights == "int8":
+        traffic, traffic_src = 15.794432e6, "ncu dram__bytes_read.sum + dram__bytes_write.sum, bytes per launch"
     # whole-step roofline (BASELINE: F = N x 2.644 GFLOP, B = W + N x 1.24 MB)
     n = args.sessions
     W = 0.659e9 if args.weights == "int8" else 1.318e9
@@ -446,7 +452,8 @@ def main():
                        "max": lat[-1]},
         "roofline": {"bound": "tensor", "kernel": f"int8-weight FFN GEMM {M}x{FULL.ffn}x{FULL.hidden}",
                      "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s", "frac": achieved / peak_tf,
-                     "traffic": None, "peak_source": f"{peak_src} bf16 burst (kernel timed alone)"},
+                     "traffic": traffic, "traffic_source": traffic_src,
+                     "peak_source": f"{peak_src} bf16 burst (kernel timed alone)"},
         "roofline_step": {"t_roof_ms": t_roof * 1e3, "t_measured_ms": ms_step, "frac": t_roof * 1e3 / ms_step,
                           "definition": "max(N*2.644 GFLOP / sustained bf16 peak, (W + N*1.24 MB) / HBM peak)"},
         "e2e": {"value": e2e_frames / e2e_s, "unit": UNIT, "h2d_bytes_per_step": res["h2d"],

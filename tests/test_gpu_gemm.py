@@ -50,7 +50,7 @@ def test_gemm_fp32_out_matches_torch(lib, M, int8):
     torch.testing.assert_close(out, ref, rtol=1e-4, atol=1e-4 * ref.abs().max().item())
 
 
-@pytest.mark.parametrize("M", [2, 130, 600])
+@pytest.mark.parametrize("M", [2, 130, 600, 2048])
 @pytest.mark.parametrize("int8", [False, True])
 def test_gemm_bf16_silu_bias_matches_torch(lib, M, int8):
     out, ref = run_gemm(lib, M, 6144, 1536, int8, 0, 1, 1, True, seed=100 + M)
