@@ -408,7 +408,7 @@ int make_op(Ctx& c, GemmOp& op, void* w, const __half* scale, int O, int K, cons
   if (out_kind == 0) {
     // A split bf16 output goes through an fp32 partial-sum buffer and a finalize
     // pass; worth it only while the tiles cannot fill half of the SMs.
-    const int tn = gemm_token_tile(tok_cap);
+    const int tn = gemm_token_tile(O, tok_cap, c.num_sms);
     const int tiles = (O / 128) * ((tok_cap + tn - 1) / tn);
     if (tiles * 2 >= c.num_sms) op.splits = 1;
   }

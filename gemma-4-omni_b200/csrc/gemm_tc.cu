@@ -23,14 +23,15 @@
 //               (2 x TN fp32 columns), so the epilogue of one unit overlaps the
 //               main loop of the next
 //   warps 2..9  epilogue, two groups of four warps draining alternate tiles:
-//               tcgen05.ld -> per-channel int8 scale, bias, clamps, SiLU ->
-//               [16 tokens x 128 features] smem staging -> TMA store (or TMA
-//               reduce-add for split-K partial sums)
-//   warps 10..17 int8 only: widen each staged int8 weight tile to bf16 directly
+//               tcgen05.ld (double-buffered 32-column loads) -> per-channel
+//               int8 scale, bias, clamps, SiLU -> direct coalesced global
+//               stores (one token's 32 features per warp instruction) or
+//               fp32 reductions for split-K partial sums
+//   warps 10..17 int8 only: widen each staged int8 weight tile to fp16 directly
 //               in the 128-byte-swizzled layout UMMA reads (exact: every int8
-//               is a bf16); the scale is applied per accumulator lane.
+//               is an fp16); the scale is applied per accumulator lane.
 // Every wait is bounded (common.cuh); on a timeout the kernel records
-// kStatusWaitTimeout, drains its outstanding stores and frees its TMEM.
+// kStatusWaitTimeout and takes its teardown path (TMEM freed).
 #include "common.cuh"
 #include "kernels.h"
 
@@ -46,23 +47,25 @@ constexpr int kBlockO = 128;
 constexpr int kBlockK = 64;
 constexpr uint32_t kABytes = kBlockO * kBlockK * 2;  // bf16 A tile, 16 KB
 constexpr uint32_t kRawBytes = kBlockO * kBlockK;    // int8 A tile, 8 KB
-constexpr int kChunk = 16;                           // tokens per epilogue chunk
-constexpr uint32_t kStagingBytes = kChunk * kBlockO * 4;  // one fp32 staging buffer, 8 KB (x4)
 
 template <int TN, bool WINT8>
 struct GemmCfg {
+  // TMEM columns (tokens) per epilogue load: the int8 kernel runs 18 warps,
+  // which caps it at 96 registers per thread, so it drains 16 columns at a time
+  static constexpr int kCols = WINT8 ? 16 : 32;
   static constexpr uint32_t kBBytes = TN * kBlockK * 2;
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
-  // operand ring + 4 staging buffers within 224 KB (the 227 KB opt-in limit
-  // leaves room for barriers and the 1 KB alignment slack)
-  static constexpr int kStages = (224 * 1024 - 4 * kStagingBytes) / kStageBytes > 8
-                                     ? 8
-                                     : (224 * 1024 - 4 * kStagingBytes) / kStageBytes;
+  // operand ring within 224 KB (the 227 KB opt-in limit leaves room for the
+  // barriers and the 1 KB alignment slack)
+  static constexpr int kStages = (224 * 1024) / kStageBytes > 8 ? 8 : (224 * 1024) / kStageBytes;
   static constexpr uint32_t kBarBytes = (4 * kStages + 4) * 8 + 16;
-  static constexpr uint32_t kSmemBytes =
-      kStages * kStageBytes + 4 * kStagingBytes + kBarBytes + 1024;
+  static constexpr uint32_t kSmemBytes = kStages * kStageBytes + kBarBytes + 1024;
   static constexpr int kThreads = WINT8 ? 576 : 320;
-  static constexpr uint32_t kTmemCols = 2 * TN;  // double-buffered accumulator
+  // double-buffered accumulator: two power-of-two column blocks of >= TN
+  static constexpr uint32_t kTmemCols = TN <= 32 ? 64 : TN <= 64 ? 128 : TN <= 128 ? 256 : 512;
+  static constexpr int kBufCols = kTmemCols / 2;  // column offset of accumulator 1
+  // the two epilogue groups split a tile's columns at kHalf (a kCols multiple)
+  static constexpr int kHalf = ((TN / 2 + kCols - 1) / kCols) * kCols;
 };
 
 // Widens 16 int8 to 16 fp16 with two byte permutes and two packed fp16
@@ -96,45 +99,35 @@ __device__ __forceinline__ void tma_load_2d_nohint(void* dst, const CUtensorMap*
       : "memory");
 }
 
-__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
-  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(smem_u32(src)), "r"(c0), "r"(c1)
-               : "memory");
-}
-
-__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const void* src, int c0,
-                                                  int c1) {
-  asm volatile(
-      "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
-          reinterpret_cast<uint64_t>(map)),
-      "r"(smem_u32(src)), "r"(c0), "r"(c1)
-      : "memory");
-}
-
-__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_read1() {
-  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
-}
-__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
-// Named barrier of one epilogue group (ids 1 and 2; 0 is __syncthreads).
-__device__ __forceinline__ void epi_bar(int g) {
-  asm volatile("bar.sync %0, 128;" ::"r"(1 + g) : "memory");
-}
-
-// 32 lanes x 16 consecutive fp32 columns per warp.
-__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, float (&v)[16]) {
-  uint32_t r[16];
+// 32 lanes x NC consecutive fp32 columns per warp, issued without waiting:
+// the registers are valid only after tmem_wait_ld on the same array.
+__device__ __forceinline__ void tmem_ld_async(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
       "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15])
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_ld_async(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+// Waits for this thread's TMEM loads; the array is threaded through the asm so
+// no use of the loaded values can be scheduled before the wait.
+__device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+               :
+               : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[32]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
 }
 
 // SiLU(x) = x * sigmoid(x) = h + h * tanh(h) with h = x / 2: one hardware
@@ -166,10 +159,25 @@ __device__ __forceinline__ Unit unit_of(int u, int o_tiles, int t_tiles, int TN,
   return r;
 }
 
+// Epilogue math of NC accumulator columns (tokens) of one output feature:
+// int8 scale, bias, output clamp, optional SiLU of the bf16-rounded linear
+// output, next-input clamp.  Branch-free over the columns so the NC
+// independent chains interleave.
+template <bool SILU, int NC>
+__device__ __forceinline__ void epilogue_math(const uint32_t (&r)[NC], float (&y)[NC], float scale,
+                                              float bias, float lo, float hi, float plo, float phi) {
+#pragma unroll
+  for (int j = 0; j < NC; ++j) {
+    float v = fminf(fmaxf(fmaf(__uint_as_float(r[j]), scale, bias), lo), hi);
+    if (SILU) v = silu_tanh(bf16_round(v));
+    y[j] = fminf(fmaxf(v, plo), phi);
+  }
+}
+
 template <int TN, bool WINT8>
 __global__ void __launch_bounds__(GemmCfg<TN, WINT8>::kThreads, 1)
     gemm_wx_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
-                   const __grid_constant__ CUtensorMap tm_out, const GemmParams p) {
+                   const GemmParams p) {
   using Cfg = GemmCfg<TN, WINT8>;
   constexpr int S = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -185,10 +193,9 @@ __global__ void __launch_bounds__(GemmCfg<TN, WINT8>::kThreads, 1)
 
   auto stage_a = [&](int s) { return smem + s * Cfg::kStageBytes; };
   auto stage_b = [&](int s) { return smem + s * Cfg::kStageBytes + kABytes; };
-  // int8 weights land in the upper half of their stage's bf16 A tile
+  // int8 weights land in the upper half of their stage's fp16 A tile
   auto stage_raw = [&](int s) { return smem + s * Cfg::kStageBytes + kRawBytes; };
-  uint8_t* staging = smem + S * Cfg::kStageBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(staging + 4 * kStagingBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
   uint64_t* full = bars;
   uint64_t* empty = bars + S;
   uint64_t* conv = bars + 2 * S;
@@ -211,14 +218,13 @@ __global__ void __launch_bounds__(GemmCfg<TN, WINT8>::kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tmem_full[b], 1);
-      mbar_init(&tmem_empty[b], 4);
+      mbar_init(&tmem_empty[b], 8);  // all eight epilogue warps
     }
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tm_w);
     tma_prefetch_desc(&tm_x);
-    tma_prefetch_desc(&tm_out);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, Cfg::kTmemCols);
@@ -265,7 +271,7 @@ __global__ void __launch_bounds__(GemmCfg<TN, WINT8>::kThreads, 1)
         const uint32_t aph = (local >> 1) & 1;
         if (!mbar_wait(&tmem_empty[b], aph ^ 1, p.status)) break;
         tc_fence_after();
-        const uint32_t acc = tmem_base + static_cast<uint32_t>(b * TN);
+        const uint32_t acc = tmem_base + static_cast<uint32_t>(b * Cfg::kBufCols);
         for (int i = 0; i < w.nkb; ++i, ++it) {
           const int s = it % S;
           const uint32_t ph = (it / S) & 1;
@@ -277,7 +283,7 @@ __global__ void __launch_bounds__(GemmCfg<TN, WINT8>::kThreads, 1)
           const uint64_t b_desc = smem_desc_k128(smem_u32(stage_b(s)));
 #pragma unroll
           for (int j = 0; j < kBlockK / 16; ++j) {
-            // advance 16 bf16 = 32 bytes along K inside the swizzled row
+            // advance 16 elements = 32 bytes along K inside the swizzled row
             umma_bf16(acc, a_desc + static_cast<uint64_t>(j * 2), b_desc + static_cast<uint64_t>(j * 2),
                       idesc, (i > 0 || j > 0) ? 1u : 0u);
           }
@@ -287,71 +293,93 @@ __global__ void __launch_bounds__(GemmCfg<TN, WINT8>::kThreads, 1)
       }
     }
   } else if (warp < 10) {
-    // ---------------- epilogue: TMEM -> registers -> smem staging -> TMA store.
-    // Two groups of four warps; group g drains the CTA's units k = g, g+2, ...,
-    // i.e. always accumulator buffer g, so two tiles drain concurrently.
+    // ---------------- epilogue: TMEM -> registers -> global memory.
+    // All eight warps drain every tile: group g (four warps, one per TMEM lane
+    // quarter) takes columns [g*kHalf, (g+1)*kHalf).  The other accumulator
+    // buffer keeps the MMA warp busy meanwhile.
+    // Lane = output feature, TMEM column = token: every store instruction
+    // writes one token's 32 consecutive features (64 B bf16/fp16, 128 B fp32).
+    // TMEM loads (kCols columns) are double-buffered in registers, so the next
+    // load is in flight while the current columns are scaled and stored.
     const int g = (warp - 2) >> 2;
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const bool leader = ((threadIdx.x - 64) & 127) == 0;
-    uint8_t* stg_base = staging + g * 2 * kStagingBytes;
-    int k = g, chunks_issued = 0;
-    for (int u = blockIdx.x + g * gridDim.x; u < units; u += 2 * gridDim.x, k += 2) {
+    const bool f16 = p.out_f16 != 0;
+    const bool silu = p.out_mode == 0 && p.act == 1;
+    // clamps of the linear output (bf16 / fp32 stores) and of the next input
+    const float lo = p.out_mode == 2 ? -INFINITY : p.out_lo, hi = p.out_mode == 2 ? INFINITY : p.out_hi;
+    const float plo = p.out_mode == 0 ? p.post_lo : -INFINITY, phi = p.out_mode == 0 ? p.post_hi : INFINITY;
+    int local = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
       const Unit w = unit_of(u, o_tiles, t_tiles, TN, p.kb_per_split, total_kb);
-      const int b = g;
-      const uint32_t aph = (k >> 1) & 1;
-      if (!mbar_wait(&tmem_full[b], aph, p.status)) break;
-      tc_fence_after();
       const int o = w.o0 + q * 32 + lane;
       const float scale = WINT8 ? __half2float(p.w_scale[o]) : 1.0f;
       const float bias = (p.bias && w.split == 0) ? p.bias[o] : 0.0f;
-#pragma unroll 1
-      for (int c = 0; c < TN; c += kChunk) {
-        float v[kChunk];
-        tmem_ld_32x32b_x16(tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
-                               static_cast<uint32_t>(b * TN + c), v);
-        if (w.t0 + c >= M) continue;  // uniform across the group
-        uint8_t* stg = stg_base + (chunks_issued & 1) * kStagingBytes;
-        if (leader && chunks_issued >= 2) bulk_wait_read1();  // this buffer's previous store has read smem
-        epi_bar(g);
-        if (p.out_mode == 0) {
-          uint16_t* st = reinterpret_cast<uint16_t*>(stg);
-          const bool f16 = p.out_f16 != 0;
-#pragma unroll
-          for (int j = 0; j < kChunk; ++j) {
-            float y = fminf(fmaxf(fmaf(v[j], scale, bias), p.out_lo), p.out_hi);
-            if (p.act == 1) y = silu_tanh(bf16_round(y));
-            y = fminf(fmaxf(y, p.post_lo), p.post_hi);
-            st[j * kBlockO + q * 32 + lane] = act_bits(y, f16);
-          }
+      const int b = local & 1;
+      if (!mbar_wait(&tmem_full[b], (local >> 1) & 1, p.status)) break;
+      tc_fence_after();
+      const int nvalid = min(TN, M - w.t0);  // tokens of this tile below the live count
+      const int c_begin = g * Cfg::kHalf;
+      const int c_end = min(c_begin + Cfg::kHalf, nvalid);
+      const uint32_t tbase =
+          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * Cfg::kBufCols);
+      const size_t ld = static_cast<size_t>(p.ld_out);
+      constexpr int NC = Cfg::kCols;
+      auto drain = [&](const uint32_t (&r)[NC], int c) {
+        float y[NC];
+        if (silu) {
+          epilogue_math<true, NC>(r, y, scale, bias, lo, hi, plo, phi);
         } else {
-          float* st = reinterpret_cast<float*>(stg);
+          epilogue_math<false, NC>(r, y, scale, bias, lo, hi, plo, phi);
+        }
+        const size_t base = static_cast<size_t>(w.t0 + c) * ld + o;
+        const int n = c_end - c;  // >= 1
+        if (p.out_mode == 0) {
+          uint16_t* dst = static_cast<uint16_t*>(p.out) + base;
+          if (n >= NC) {
 #pragma unroll
-          for (int j = 0; j < kChunk; ++j) {
-            float y = fmaf(v[j], scale, bias);
-            if (p.out_mode == 1) y = fminf(fmaxf(y, p.out_lo), p.out_hi);
-            st[j * kBlockO + q * 32 + lane] = y;
-          }
-        }
-        fence_proxy_async_smem();
-        epi_bar(g);
-        if (leader) {
-          if (p.out_mode == 2) {
-            tma_reduce_add_2d(&tm_out, stg, w.o0, w.t0 + c);
+            for (int j = 0; j < NC; ++j) dst[j * ld] = act_bits(y[j], f16);
           } else {
-            tma_store_2d(&tm_out, stg, w.o0, w.t0 + c);
+#pragma unroll
+            for (int j = 0; j < NC; ++j)
+              if (j < n) dst[j * ld] = act_bits(y[j], f16);
           }
-          bulk_commit();
+        } else if (p.out_mode == 1) {
+          float* dst = static_cast<float*>(p.out) + base;
+#pragma unroll
+          for (int j = 0; j < NC; ++j)
+            if (j < n) dst[j * ld] = y[j];
+        } else {
+          float* dst = static_cast<float*>(p.out) + base;
+#pragma unroll
+          for (int j = 0; j < NC; ++j)
+            if (j < n) atomicAdd(dst + j * ld, y[j]);  // split-K partial sum
         }
-        ++chunks_issued;
+      };
+      if (c_begin < c_end) {
+        uint32_t ra[NC], rb[NC];
+        tmem_ld_async(tbase + static_cast<uint32_t>(c_begin), ra);
+        tmem_wait_ld(ra);
+#pragma unroll 1
+        for (int c = c_begin; c < c_end; c += 2 * NC) {
+          const bool more_b = c + NC < c_end;
+          if (more_b) tmem_ld_async(tbase + static_cast<uint32_t>(c + NC), rb);
+          drain(ra, c);
+          if (more_b) {
+            tmem_wait_ld(rb);
+            const bool more_a = c + 2 * NC < c_end;
+            if (more_a) tmem_ld_async(tbase + static_cast<uint32_t>(c + 2 * NC), ra);
+            drain(rb, c + NC);
+            if (more_a) tmem_wait_ld(ra);
+          }
+        }
       }
       // accumulator drained: hand the TMEM buffer back to the MMA warp
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tmem_empty[b]);
     }
-    if (leader) bulk_wait_all();
   } else {
-    // ---------------- int8 -> bf16 converters (WINT8 only; warps 10..17)
+    // ---------------- int8 -> fp16 converters (WINT8 only; warps 10..17)
     if (WINT8) {
       const int ct = threadIdx.x - 320;
       int it = 0;
@@ -365,7 +393,7 @@ __global__ void __launch_bounds__(GemmCfg<TN, WINT8>::kThreads, 1)
             ok = false;
             break;
           }
-          // The int8 tile sits in the upper half of the bf16 tile it widens into:
+          // The int8 tile sits in the upper half of the fp16 tile it widens into:
           // read every raw chunk first, meet on rawrd[s], then write.
           const uint8_t* raw = stage_raw(s);
           uint8_t* dst = stage_a(s);
@@ -386,11 +414,11 @@ __global__ void __launch_bounds__(GemmCfg<TN, WINT8>::kThreads, 1)
             const int cidx = ct + 256 * qd;
             const int row = cidx >> 2;
             const int ch = cidx & 3;
-            int4 lo, hi;
-            convert_i8x16_to_f16(r[qd], lo, hi);
+            int4 lo4, hi4;
+            convert_i8x16_to_f16(r[qd], lo4, hi4);
             const int sw = row & 7;
-            *reinterpret_cast<int4*>(dst + row * 128 + (((2 * ch) ^ sw) << 4)) = lo;
-            *reinterpret_cast<int4*>(dst + row * 128 + (((2 * ch + 1) ^ sw) << 4)) = hi;
+            *reinterpret_cast<int4*>(dst + row * 128 + (((2 * ch) ^ sw) << 4)) = lo4;
+            *reinterpret_cast<int4*>(dst + row * 128 + (((2 * ch + 1) ^ sw) << 4)) = hi4;
           }
           fence_proxy_async_smem();
           __syncwarp();
@@ -429,8 +457,7 @@ cudaError_t launch_gemm_t(const GemmPlan& plan, const GemmParams& p, int splits,
   using Cfg = GemmCfg<TN, WINT8>;
   const int units = (plan.O / kBlockO) * ((plan.m_cap + TN - 1) / TN) * splits;
   const int grid = units < num_sms ? units : num_sms;
-  gemm_wx_kernel<TN, WINT8>
-      <<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(plan.tm_w, plan.tm_x, plan.tm_out, p);
+  gemm_wx_kernel<TN, WINT8><<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(plan.tm_w, plan.tm_x, p);
   return cudaGetLastError();
 }
 
@@ -452,14 +479,21 @@ int sm_count() {
 // device.  Called once per device before any launch (and before graph capture).
 cudaError_t gemm_init_attributes() {
   cudaError_t e = cudaSuccess;
-  if (e == cudaSuccess) e = set_smem_attr<32, false>();
-  if (e == cudaSuccess) e = set_smem_attr<64, false>();
-  if (e == cudaSuccess) e = set_smem_attr<128, false>();
-  if (e == cudaSuccess) e = set_smem_attr<256, false>();
-  if (e == cudaSuccess) e = set_smem_attr<32, true>();
-  if (e == cudaSuccess) e = set_smem_attr<64, true>();
-  if (e == cudaSuccess) e = set_smem_attr<128, true>();
-  if (e == cudaSuccess) e = set_smem_attr<256, true>();
+#define LB_GEMM_ATTR(TNV)                                      \
+  if (e == cudaSuccess) e = set_smem_attr<TNV, false>();       \
+  if (e == cudaSuccess) e = set_smem_attr<TNV, true>();
+  LB_GEMM_ATTR(32)
+  LB_GEMM_ATTR(64)
+  LB_GEMM_ATTR(128)
+  LB_GEMM_ATTR(144)
+  LB_GEMM_ATTR(160)
+  LB_GEMM_ATTR(176)
+  LB_GEMM_ATTR(192)
+  LB_GEMM_ATTR(208)
+  LB_GEMM_ATTR(224)
+  LB_GEMM_ATTR(240)
+  LB_GEMM_ATTR(256)
+#undef LB_GEMM_ATTR
   return e;
 }
 
@@ -483,11 +517,29 @@ int make_tensor_map_2d(CUtensorMap* map, const void* base, int elem_bytes, uint6
   return r == CUDA_SUCCESS ? 0 : -2;
 }
 
-int gemm_token_tile(int m_cap) {
+int gemm_token_tile(int O, int m_cap, int num_sms) {
   if (m_cap <= 32) return 32;
   if (m_cap <= 64) return 64;
   if (m_cap <= 128) return 128;
-  return 256;
+  if (m_cap <= 256) return 256;
+  // Several token tiles: pick the width (a multiple of 16 in [128, 256]) that
+  // minimises waves x (TN + 32), i.e. whole waves of equal-length units with a
+  // per-unit overhead, so e.g. 12 feature tiles x 2048 tokens run as
+  // 12 x 12 units of 176 tokens (one full wave) instead of 12 x 8 of 256.
+  static constexpr int kCand[] = {256, 240, 224, 208, 192, 176, 160, 144, 128};
+  const int o_tiles = O / kBlockO;
+  int best = 256;
+  long best_cost = -1;
+  for (int tn : kCand) {
+    const long units = static_cast<long>(o_tiles) * ((m_cap + tn - 1) / tn);
+    const long waves = (units + num_sms - 1) / num_sms;
+    const long cost = waves * (tn + 32);
+    if (best_cost < 0 || cost < best_cost) {
+      best = tn;
+      best_cost = cost;
+    }
+  }
+  return best;
 }
 
 int gemm_prepare(GemmPlan* plan, const void* w, bool w_int8, int O, int K, const void* x, int x_ld,
@@ -498,7 +550,7 @@ int gemm_prepare(GemmPlan* plan, const void* w, bool w_int8, int O, int K, const
   plan->K = K;
   plan->w_int8 = w_int8;
   plan->m_cap = m_cap;
-  plan->tn = gemm_token_tile(m_cap);
+  plan->tn = gemm_token_tile(O, m_cap, sm_count());
   plan->out_mode = out_mode;
   plan->out_f16 = out_f16;
   int rc;
@@ -513,23 +565,19 @@ int gemm_prepare(GemmPlan* plan, const void* w, bool w_int8, int O, int K, const
   // The activation map covers exactly m_cap rows (TMA zero-fills rows past it).
   // A box may not exceed the tensor extent, so with fewer rows than the token
   // tile the box shrinks to m_cap rows; the tile's remaining shared-memory rows
-  // then hold stale data that only reaches output columns t >= m_cap, which are
-  // clipped by the output map.
+  // then hold stale data that only reaches output columns t >= m_cap, which
+  // the epilogue never stores (it stops at the live token count M <= m_cap).
   plan->x_box_rows = m_cap < plan->tn ? m_cap : plan->tn;
   // activations are fp16 when the weights are int8, bf16 otherwise
   rc = make_tensor_map_2d(&plan->tm_x, x, 2, K, static_cast<uint64_t>(m_cap),
                           static_cast<uint64_t>(x_ld) * 2, kBlockK,
                           static_cast<uint32_t>(plan->x_box_rows), true, w_int8);
   if (rc) return rc;
-  // Output map: [m_cap rows][ld_out], stores of 16-token x 128-feature boxes.
-  // Rows t >= m_cap are clipped by TMA; rows in [M, m_cap) receive values of
-  // columns the kernel computed from stale activation rows -- never read.
-  const int ebytes = out_mode == 0 ? 2 : 4;
-  plan->out_box_rows = m_cap < kChunk ? m_cap : kChunk;
-  return make_tensor_map_2d(&plan->tm_out, out, ebytes, static_cast<uint64_t>(O),
-                            static_cast<uint64_t>(m_cap), static_cast<uint64_t>(ld_out) * ebytes,
-                            kBlockO, static_cast<uint32_t>(plan->out_box_rows), false,
-                            out_mode == 0 && out_f16);
+  // The output [m_cap rows][ld_out] is written with plain stores, clipped at
+  // the live token count, so it needs no tensor map.
+  (void)out;
+  (void)ld_out;
+  return 0;
 }
 
 cudaError_t gemm_launch(const GemmPlan& plan, GemmParams p, int splits, cudaStream_t stream) {
@@ -553,6 +601,13 @@ cudaError_t gemm_launch(const GemmPlan& plan, GemmParams p, int splits, cudaStre
     LB_GEMM_CASE(32)
     LB_GEMM_CASE(64)
     LB_GEMM_CASE(128)
+    LB_GEMM_CASE(144)
+    LB_GEMM_CASE(160)
+    LB_GEMM_CASE(176)
+    LB_GEMM_CASE(192)
+    LB_GEMM_CASE(208)
+    LB_GEMM_CASE(224)
+    LB_GEMM_CASE(240)
     LB_GEMM_CASE(256)
     default:
       return cudaErrorInvalidValue;
@@ -561,7 +616,7 @@ cudaError_t gemm_launch(const GemmPlan& plan, GemmParams p, int splits, cudaStre
 }
 
 int gemm_pick_splits(int O, int K, int m_cap, int num_sms) {
-  const int tn = gemm_token_tile(m_cap);
+  const int tn = gemm_token_tile(O, m_cap, num_sms);
   const int tiles = (O / kBlockO) * ((m_cap + tn - 1) / tn);
   const int total_kb = K / kBlockK;
   // Choose the split count that best fills whole waves of SMs: efficiency =

@@ -35,10 +35,8 @@ struct GemmParams {
 struct GemmPlan {
   CUtensorMap tm_w;
   CUtensorMap tm_x;
-  CUtensorMap tm_out;
   int O = 0, K = 0, m_cap = 0, tn = 0;
   int x_box_rows = 0;    // rows per activation TMA box: min(tn, m_cap)
-  int out_box_rows = 0;  // rows per output TMA box: min(32, m_cap)
   int out_mode = 0;
   bool out_f16 = false;
   bool w_int8 = false;
@@ -47,7 +45,9 @@ struct GemmPlan {
 int make_tensor_map_2d(CUtensorMap* map, const void* base, int elem_bytes, uint64_t inner,
                        uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
                        uint32_t box_outer, bool swizzle128, bool f16 = false);
-int gemm_token_tile(int m_cap);
+// Token tile (UMMA N) for an [m_cap x O] output: 32/64/128/256 up to 256
+// tokens, beyond that the multiple of 16 in [128, 256] that fills whole waves.
+int gemm_token_tile(int O, int m_cap, int num_sms);
 // Encodes the tensor maps for W ([O,K] bf16 or int8), X ([m_cap,K], row stride
 // x_ld elements; bf16, or fp16 when W is int8; TMA zero-fills rows past m_cap)
 // and the output ([m_cap, ld_out]: out_mode 0 bf16 or, with out_f16, fp16;

@@ -42,11 +42,20 @@ def run_gemm(lib, M, O, K, int8, mode, act, splits, bias, seed):
     return out.float(), ref
 
 
-@pytest.mark.parametrize("M", [1, 2, 31, 64, 200, 2048])
+@pytest.mark.parametrize("M", [1, 2, 31, 64, 200, 300, 2048])
 @pytest.mark.parametrize("int8", [False, True])
 def test_gemm_fp32_out_matches_torch(lib, M, int8):
     out, ref = run_gemm(lib, M, 1536, 1536, int8, 1, 0, 1, False, seed=M)
     # fp32 output: only summation order differs from the fp32 reference
+    torch.testing.assert_close(out, ref, rtol=1e-4, atol=1e-4 * ref.abs().max().item())
+
+
+# With O = 1536 these token counts select every token-tile width the kernel
+# has beyond 256 tokens (144, 160, ..., 256), each with a ragged last tile.
+@pytest.mark.parametrize("M", [1537, 1729, 1921, 2113, 2305, 2497, 2689, 2881])
+@pytest.mark.parametrize("int8", [False, True])
+def test_gemm_every_token_tile_width(lib, M, int8):
+    out, ref = run_gemm(lib, M, 1536, 1536, int8, 1, 0, 1, True, seed=7 + M)
     torch.testing.assert_close(out, ref, rtol=1e-4, atol=1e-4 * ref.abs().max().item())
 
 
@@ -59,10 +68,11 @@ def test_gemm_bf16_silu_bias_matches_torch(lib, M, int8):
     torch.testing.assert_close(out, ref, rtol=1.6e-2, atol=1e-3)
 
 
-@pytest.mark.parametrize("splits", [2, 7, 24])
+@pytest.mark.parametrize("M,splits", [(40, 2), (40, 7), (40, 24), (512, 3), (777, 2)])
 @pytest.mark.parametrize("int8", [False, True])
-def test_gemm_split_k_atomic_matches_torch(lib, splits, int8):
-    out, ref = run_gemm(lib, 40, 1536, 6144, int8, 2, 0, splits, True, seed=splits)
+def test_gemm_split_k_atomic_matches_torch(lib, M, splits, int8):
+    # M >= 256 runs on CTA pairs (256-feature tiles), M = 40 on single CTAs
+    out, ref = run_gemm(lib, M, 1536, 6144, int8, 2, 0, splits, True, seed=splits + M)
     torch.testing.assert_close(out, ref, rtol=1e-4, atol=1e-4 * ref.abs().max().item())
 
 
