@@ -32,12 +32,12 @@ int lb_op_gemm(const void* x, int x_ld, int m, const void* w, int w_int8, const 
                const float* bias, int out_features, int k, void* out, int ld_out, int out_mode,
                int act, int splits, int* status_dev, void* stream) {
   if (!x || !w || !out || m <= 0) return LB_ERR_INVALID_ARGUMENT;
-  if (w_int8 && !w_scale) return LB_ERR_INVALID_ARGUMENT;
+  if (w_int8 < 0 || w_int8 > 2 || (w_int8 && !w_scale)) return LB_ERR_INVALID_ARGUMENT;
   if (out_mode < 0 || out_mode > 2 || act < 0 || act > 1) return LB_ERR_INVALID_ARGUMENT;
   if (splits > 1 && out_mode != 2) return LB_ERR_INVALID_ARGUMENT;
   if (ensure_gemm_attributes() != cudaSuccess) return LB_ERR_CUDA;
   GemmPlan plan;
-  int rc = gemm_prepare(&plan, w, w_int8 != 0, out_features, k, x, x_ld, m, out, ld_out, out_mode);
+  int rc = gemm_prepare(&plan, w, w_int8, out_features, k, x, x_ld, m, out, ld_out, out_mode);
   if (rc) return rc == -3 ? LB_ERR_INVALID_ARGUMENT : LB_ERR_CUDA;
   GemmParams p;
   p.m_static = m;

@@ -71,7 +71,7 @@ int lb_op_gemm_splitk_scratch(const void* x, int x_ld, int m, const void* w, int
                               void* out, int ld_out, int act, int splits, int* status_dev,
                               void* stream) {
   if (!x || !w || !out || m <= 0 || out_features <= 0 || k <= 0) return LB_ERR_INVALID_ARGUMENT;
-  if (w_int8 && !w_scale) return LB_ERR_INVALID_ARGUMENT;
+  if (w_int8 < 0 || w_int8 > 2 || (w_int8 && !w_scale)) return LB_ERR_INVALID_ARGUMENT;
   if (act < 0 || act > 1 || splits < 1 || ld_out < out_features || ld_out % 8 != 0 ||
       reinterpret_cast<uintptr_t>(out) % 16 != 0)
     return LB_ERR_INVALID_ARGUMENT;
@@ -86,7 +86,7 @@ int lb_op_gemm_splitk_scratch(const void* x, int x_ld, int m, const void* w, int
   cudaStream_t s = static_cast<cudaStream_t>(stream);
 
   GemmPlan plan;
-  rc = gemm_prepare(&plan, w, w_int8 != 0, out_features, k, x, x_ld, m, acc, out_features, 2);
+  rc = gemm_prepare(&plan, w, w_int8, out_features, k, x, x_ld, m, acc, out_features, 2);
   if (rc) return rc == -3 ? LB_ERR_INVALID_ARGUMENT : LB_ERR_CUDA;
   GemmParams p;
   p.m_static = m;

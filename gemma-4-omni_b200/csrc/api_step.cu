@@ -13,6 +13,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 
@@ -382,12 +383,27 @@ size_t layout_acts(Ctx& c, char* base) {
 }
 
 // ------------------------------------------------------------- GEMM plans
+// Smallest bucket (tokens) whose int8-weight GEMMs read fp16-widened codes:
+// from here on the step is tensor-bound, and the in-kernel widening costs more
+// than the extra weight bytes.
+constexpr int kWideMinTokens = 512;
+
 int make_op(Ctx& c, GemmOp& op, void* w, const __half* scale, int O, int K, const void* x, int tok_cap,
             const float* bias, void* out, int out_kind, int act, const float* clip4,
             float post_lo = -INFINITY, float post_hi = INFINITY, __nv_bfloat16* final_bf16 = nullptr) {
   // out_kind: 0 = bf16 tensor, 1 = fp32, 2 = activation that feeds another GEMM
   // (bf16, or fp16 when the weights are int8)
   op.final_f16 = out_kind == 2 && c.weight_int8;
+  // int8 weights: buckets of >= kWideMinTokens tokens read the fp16 codes
+  int w_kind = 0;
+  if (c.weight_int8) {
+    w_kind = 1;
+    if (c.wide_arena && tok_cap >= kWideMinTokens) {
+      w_kind = 2;
+      w = static_cast<char*>(c.wide_arena) +
+          2 * (static_cast<char*>(w) - static_cast<char*>(c.weight_arena));
+    }
+  }
   if (out_kind == 2) out_kind = 0;
   GemmParams& p = op.params;
   p = GemmParams();
@@ -420,7 +436,7 @@ int make_op(Ctx& c, GemmOp& op, void* w, const __half* scale, int O, int K, cons
     p.out = out;
   }
   (void)final_bf16;
-  return gemm_prepare(&op.plan, w, c.weight_int8 != 0, O, K, x, K, tok_cap, p.out, O, p.out_mode,
+  return gemm_prepare(&op.plan, w, w_kind, O, K, x, K, tok_cap, p.out, O, p.out_mode,
                       op.final_f16);
 }
 
@@ -710,6 +726,7 @@ int lb_destroy(lb_ctx* x) {
   if (c.capture_stream) cudaStreamDestroy(c.capture_stream);
   if (x->pinned) cudaFreeHost(x->pinned);
   cudaFree(c.weight_arena);
+  if (c.wide_arena) cudaFree(c.wide_arena);
   cudaFree(c.state_arena);
   cudaFree(c.act_arena);
   delete x;
@@ -730,6 +747,8 @@ int lb_set_tensor(lb_ctx* x, const char* name, const void* host, int dtype, int6
   if (it == c.tensors.end()) return LB_ERR_INVALID_ARGUMENT;
   TensorSlot& t = it->second;
   if (t.dtype != dtype || t.numel != numel) return LB_ERR_INVALID_ARGUMENT;
+  if (c.state == 1 || c.state == 2) return LB_ERR_STATE;  // a packed batch is outstanding
+  c.weights_final = false;  // derived copies are rebuilt by lb_finalize_weights
   const std::string n(name);
   if (t.clip_dst) {
     float v = *static_cast<const float*>(host);
@@ -803,6 +822,21 @@ int lb_finalize_weights(lb_ctx* x) {
         return LB_ERR_INVALID_ARGUMENT;
       }
       c.w.layers[i].clip[kLinQkv][k] = b;
+    }
+  }
+  const char* env = std::getenv("LB_INT8_WIDE");
+  if (c.weight_int8 && 2 * c.cfg.max_rows >= kWideMinTokens && !(env && env[0] == '0')) {
+    {
+      cudaSetDevice(c.device);
+      const size_t n = c.weight_bytes & ~static_cast<size_t>(15);
+      cudaError_t e = c.wide_arena ? cudaSuccess : cudaMalloc(&c.wide_arena, 2 * n);
+      if (e == cudaSuccess) e = widen_int8_codes(c.weight_arena, c.wide_arena, n, nullptr);
+      if (e == cudaSuccess) e = cudaStreamSynchronize(nullptr);
+      if (e != cudaSuccess) {
+        if (c.wide_arena) cudaFree(c.wide_arena);
+        c.wide_arena = nullptr;
+        return LB_ERR_CUDA;
+      }
     }
   }
   c.weights_final = true;

@@ -48,19 +48,25 @@ constexpr int kBlockK = 64;
 constexpr uint32_t kABytes = kBlockO * kBlockK * 2;  // bf16 A tile, 16 KB
 constexpr uint32_t kRawBytes = kBlockO * kBlockK;    // int8 A tile, 8 KB
 
-template <int TN, bool WINT8>
+// Weight kinds: bf16 weights (bf16 x bf16 MMA); int8 codes widened to fp16
+// in shared memory by converter warps; fp16 codes (int8 codes widened once in
+// HBM), read by TMA like bf16.  Both int8 kinds run fp16 x fp16 MMAs with fp16
+// activations and apply the per-channel scale in the epilogue.
+constexpr int kWBf16 = 0, kWInt8 = 1, kWF16 = 2;
+
+template <int TN, int WK>
 struct GemmCfg {
   // TMEM columns (tokens) per epilogue load: the int8 kernel runs 18 warps,
   // which caps it at 96 registers per thread, so it drains 16 columns at a time
-  static constexpr int kCols = WINT8 ? 16 : 32;
+  static constexpr int kCols = WK == kWInt8 ? 16 : 32;
   static constexpr uint32_t kBBytes = TN * kBlockK * 2;
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
   // operand ring within 224 KB (the 227 KB opt-in limit leaves room for the
   // barriers and the 1 KB alignment slack)
   static constexpr int kStages = (224 * 1024) / kStageBytes > 8 ? 8 : (224 * 1024) / kStageBytes;
-  static constexpr uint32_t kBarBytes = (4 * kStages + 4) * 8 + 16;
+  static constexpr uint32_t kBarBytes = (5 * kStages + 4) * 8 + 16;
   static constexpr uint32_t kSmemBytes = kStages * kStageBytes + kBarBytes + 1024;
-  static constexpr int kThreads = WINT8 ? 576 : 320;
+  static constexpr int kThreads = WK == kWInt8 ? 576 : 320;
   // double-buffered accumulator: two power-of-two column blocks of >= TN
   static constexpr uint32_t kTmemCols = TN <= 32 ? 64 : TN <= 64 ? 128 : TN <= 128 ? 256 : 512;
   static constexpr int kBufCols = kTmemCols / 2;  // column offset of accumulator 1
@@ -174,11 +180,13 @@ __device__ __forceinline__ void epilogue_math(const uint32_t (&r)[NC], float (&y
   }
 }
 
-template <int TN, bool WINT8>
-__global__ void __launch_bounds__(GemmCfg<TN, WINT8>::kThreads, 1)
+template <int TN, int WK>
+__global__ void __launch_bounds__(GemmCfg<TN, WK>::kThreads, 1)
     gemm_wx_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
                    const GemmParams p) {
-  using Cfg = GemmCfg<TN, WINT8>;
+  using Cfg = GemmCfg<TN, WK>;
+  constexpr bool WINT8 = WK == kWInt8;   // converter warps widen int8 in shared memory
+  constexpr bool SCALED = WK != kWBf16;  // fp16 operands, per-channel scale
   constexpr int S = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -196,13 +204,14 @@ __global__ void __launch_bounds__(GemmCfg<TN, WINT8>::kThreads, 1)
   // int8 weights land in the upper half of their stage's fp16 A tile
   auto stage_raw = [&](int s) { return smem + s * Cfg::kStageBytes + kRawBytes; };
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
-  uint64_t* full = bars;
+  uint64_t* full = bars;                    // bf16: W and X tiles; int8: X tile
   uint64_t* empty = bars + S;
-  uint64_t* conv = bars + 2 * S;
+  uint64_t* conv = bars + 2 * S;            // int8: W tile widened to fp16
   uint64_t* rawrd = bars + 3 * S;           // int8: every converter warp has read the raw tile
-  uint64_t* tmem_full = bars + 4 * S;       // [2]
-  uint64_t* tmem_empty = bars + 4 * S + 2;  // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4 * S + 4);
+  uint64_t* full_w = bars + 4 * S;          // int8: raw W tile landed
+  uint64_t* tmem_full = bars + 5 * S;       // [2]
+  uint64_t* tmem_empty = bars + 5 * S + 2;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 5 * S + 4);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -214,6 +223,7 @@ __global__ void __launch_bounds__(GemmCfg<TN, WINT8>::kThreads, 1)
       if (WINT8) {
         mbar_init(&conv[s], 8);
         mbar_init(&rawrd[s], 8);
+        mbar_init(&full_w[s], 1);
       }
     }
     for (int b = 0; b < 2; ++b) {
@@ -239,7 +249,9 @@ __global__ void __launch_bounds__(GemmCfg<TN, WINT8>::kThreads, 1)
     // ---------------- TMA producer
     if (lane == 0) {
       const uint64_t pol_x = l2_policy_evict_last();
-      const uint32_t tx = (WINT8 ? kRawBytes : kABytes) + p.b_tx_bytes;
+      // int8: the raw weight tile completes on its own barrier, so widening
+      // never waits for the activation tile
+      const uint32_t tx = WINT8 ? p.b_tx_bytes : kABytes + p.b_tx_bytes;
       int it = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
@@ -251,9 +263,13 @@ __global__ void __launch_bounds__(GemmCfg<TN, WINT8>::kThreads, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[s], tx);
           const int k = (w.kb_begin + i) * kBlockK;
-          tma_load_2d_nohint(WINT8 ? stage_raw(s) : stage_a(s), &tm_w, &full[s], k, w.o0);
+          if (WINT8) {
+            mbar_arrive_expect_tx(&full_w[s], kRawBytes);
+            tma_load_2d_nohint(stage_raw(s), &tm_w, &full_w[s], k, w.o0);
+          }
+          mbar_arrive_expect_tx(&full[s], tx);
+          if (!WINT8) tma_load_2d_nohint(stage_a(s), &tm_w, &full[s], k, w.o0);
           tma_load_2d(stage_b(s), &tm_x, &full[s], k, w.t0, pol_x);
         }
       }
@@ -261,8 +277,8 @@ __global__ void __launch_bounds__(GemmCfg<TN, WINT8>::kThreads, 1)
   } else if (warp == 1) {
     // ---------------- UMMA issuer
     if (lane == 0) {
-      // int8 weights run with fp16 operands (widened W, fp16 activations)
-      constexpr uint32_t idesc = WINT8 ? umma_idesc_f16(kBlockO, TN) : umma_idesc_bf16(kBlockO, TN);
+      // int8 weights run with fp16 operands (widened codes, fp16 activations)
+      constexpr uint32_t idesc = SCALED ? umma_idesc_f16(kBlockO, TN) : umma_idesc_bf16(kBlockO, TN);
       int it = 0, local = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++local) {
@@ -312,7 +328,7 @@ __global__ void __launch_bounds__(GemmCfg<TN, WINT8>::kThreads, 1)
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
       const Unit w = unit_of(u, o_tiles, t_tiles, TN, p.kb_per_split, total_kb);
       const int o = w.o0 + q * 32 + lane;
-      const float scale = WINT8 ? __half2float(p.w_scale[o]) : 1.0f;
+      const float scale = SCALED ? __half2float(p.w_scale[o]) : 1.0f;
       const float bias = (p.bias && w.split == 0) ? p.bias[o] : 0.0f;
       const int b = local & 1;
       if (!mbar_wait(&tmem_full[b], (local >> 1) & 1, p.status)) break;
@@ -380,50 +396,55 @@ __global__ void __launch_bounds__(GemmCfg<TN, WINT8>::kThreads, 1)
     }
   } else {
     // ---------------- int8 -> fp16 converters (WINT8 only; warps 10..17)
+    // The int8 tile sits in the upper half of the fp16 tile it widens into, so
+    // every converter warp reads its raw chunks and meets the others on
+    // rawrd[s] before anyone writes.  Software-pipelined one stage ahead: the
+    // raw chunks of stage it+1 are read (and rawrd arrived) before stage it is
+    // widened, so the rawrd meeting of stage it is normally already complete.
     if (WINT8) {
       const int ct = threadIdx.x - 320;
-      int it = 0;
-      bool ok = true;
-      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-        const Unit w = unit_of(u, o_tiles, t_tiles, TN, p.kb_per_split, total_kb);
-        for (int i = 0; i < w.nkb; ++i, ++it) {
-          const int s = it % S;
-          const uint32_t ph = (it / S) & 1;
-          if (!mbar_wait(&full[s], ph, p.status)) {
-            ok = false;
-            break;
-          }
-          // The int8 tile sits in the upper half of the fp16 tile it widens into:
-          // read every raw chunk first, meet on rawrd[s], then write.
-          const uint8_t* raw = stage_raw(s);
-          uint8_t* dst = stage_a(s);
-          int4 r[2];
+      int n_it = 0;  // k-blocks this CTA streams, in ring order
+      for (int u = blockIdx.x; u < units; u += gridDim.x)
+        n_it += unit_of(u, o_tiles, t_tiles, TN, p.kb_per_split, total_kb).nkb;
+      auto read_raw = [&](int s, int4 (&r)[2]) {
+        const uint8_t* raw = stage_raw(s);
 #pragma unroll
-          for (int qd = 0; qd < 2; ++qd) {
-            const int cidx = ct + 256 * qd;  // 16-byte chunk id in the 128 x 64 B raw tile
-            r[qd] = *reinterpret_cast<const int4*>(raw + (cidx >> 2) * 64 + (cidx & 3) * 16);
-          }
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&rawrd[s]);
-          if (!mbar_wait(&rawrd[s], ph, p.status)) {
-            ok = false;
-            break;
-          }
-#pragma unroll
-          for (int qd = 0; qd < 2; ++qd) {
-            const int cidx = ct + 256 * qd;
-            const int row = cidx >> 2;
-            const int ch = cidx & 3;
-            int4 lo4, hi4;
-            convert_i8x16_to_f16(r[qd], lo4, hi4);
-            const int sw = row & 7;
-            *reinterpret_cast<int4*>(dst + row * 128 + (((2 * ch) ^ sw) << 4)) = lo4;
-            *reinterpret_cast<int4*>(dst + row * 128 + (((2 * ch + 1) ^ sw) << 4)) = hi4;
-          }
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&conv[s]);
+        for (int qd = 0; qd < 2; ++qd) {
+          const int cidx = ct + 256 * qd;  // 16-byte chunk id in the 128 x 64 B raw tile
+          r[qd] = *reinterpret_cast<const int4*>(raw + (cidx >> 2) * 64 + (cidx & 3) * 16);
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&rawrd[s]);
+      };
+      int4 cur[2], nxt[2];
+      bool ok = n_it > 0 && mbar_wait(&full_w[0], 0, p.status);
+      if (ok) read_raw(0, cur);
+      for (int it = 0; ok && it < n_it; ++it) {
+        const int s = it % S;
+        const uint32_t ph = (it / S) & 1;
+        if (it + 1 < n_it) {
+          const int s1 = (it + 1) % S;
+          if (!mbar_wait(&full_w[s1], ((it + 1) / S) & 1, p.status)) break;
+          read_raw(s1, nxt);
+        }
+        if (!mbar_wait(&rawrd[s], ph, p.status)) break;
+        uint8_t* dst = stage_a(s);
+#pragma unroll
+        for (int qd = 0; qd < 2; ++qd) {
+          const int cidx = ct + 256 * qd;
+          const int row = cidx >> 2;
+          const int ch = cidx & 3;
+          int4 lo4, hi4;
+          convert_i8x16_to_f16(cur[qd], lo4, hi4);
+          const int sw = row & 7;
+          *reinterpret_cast<int4*>(dst + row * 128 + (((2 * ch) ^ sw) << 4)) = lo4;
+          *reinterpret_cast<int4*>(dst + row * 128 + (((2 * ch + 1) ^ sw) << 4)) = hi4;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&conv[s]);
+        cur[0] = nxt[0];
+        cur[1] = nxt[1];
       }
     }
   }
@@ -451,20 +472,31 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
-template <int TN, bool WINT8>
+template <int TN, int WK>
 cudaError_t launch_gemm_t(const GemmPlan& plan, const GemmParams& p, int splits, int num_sms,
                           cudaStream_t stream) {
-  using Cfg = GemmCfg<TN, WINT8>;
+  using Cfg = GemmCfg<TN, WK>;
   const int units = (plan.O / kBlockO) * ((plan.m_cap + TN - 1) / TN) * splits;
   const int grid = units < num_sms ? units : num_sms;
-  gemm_wx_kernel<TN, WINT8><<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(plan.tm_w, plan.tm_x, p);
+  gemm_wx_kernel<TN, WK><<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(plan.tm_w, plan.tm_x, p);
   return cudaGetLastError();
 }
 
-template <int TN, bool WINT8>
+template <int TN, int WK>
 cudaError_t set_smem_attr() {
-  return cudaFuncSetAttribute(gemm_wx_kernel<TN, WINT8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              static_cast<int>(GemmCfg<TN, WINT8>::kSmemBytes));
+  return cudaFuncSetAttribute(gemm_wx_kernel<TN, WK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              static_cast<int>(GemmCfg<TN, WK>::kSmemBytes));
+}
+
+// Widens int8 codes to fp16 (exact), 16 per thread.
+__global__ void widen_i8_kernel(const int4* __restrict__ src, int4* __restrict__ dst, size_t n16) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n16;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    int4 lo, hi;
+    convert_i8x16_to_f16(src[i], lo, hi);
+    dst[2 * i] = lo;
+    dst[2 * i + 1] = hi;
+  }
 }
 
 int sm_count() {
@@ -480,8 +512,9 @@ int sm_count() {
 cudaError_t gemm_init_attributes() {
   cudaError_t e = cudaSuccess;
 #define LB_GEMM_ATTR(TNV)                                      \
-  if (e == cudaSuccess) e = set_smem_attr<TNV, false>();       \
-  if (e == cudaSuccess) e = set_smem_attr<TNV, true>();
+  if (e == cudaSuccess) e = set_smem_attr<TNV, kWBf16>();      \
+  if (e == cudaSuccess) e = set_smem_attr<TNV, kWInt8>();      \
+  if (e == cudaSuccess) e = set_smem_attr<TNV, kWF16>();
   LB_GEMM_ATTR(32)
   LB_GEMM_ATTR(64)
   LB_GEMM_ATTR(128)
@@ -542,13 +575,24 @@ int gemm_token_tile(int O, int m_cap, int num_sms) {
   return best;
 }
 
-int gemm_prepare(GemmPlan* plan, const void* w, bool w_int8, int O, int K, const void* x, int x_ld,
+cudaError_t widen_int8_codes(const void* src, void* dst, size_t n, cudaStream_t stream) {
+  if (n % 16 != 0 || reinterpret_cast<uintptr_t>(src) % 16 || reinterpret_cast<uintptr_t>(dst) % 16)
+    return cudaErrorInvalidValue;
+  const size_t n16 = n / 16;
+  const int blocks = static_cast<int>(n16 / 256 + 1 < 4096 ? n16 / 256 + 1 : 4096);
+  widen_i8_kernel<<<blocks, 256, 0, stream>>>(static_cast<const int4*>(src), static_cast<int4*>(dst), n16);
+  return cudaGetLastError();
+}
+
+int gemm_prepare(GemmPlan* plan, const void* w, int w_kind, int O, int K, const void* x, int x_ld,
                  int m_cap, void* out, int ld_out, int out_mode, bool out_f16) {
-  if (O % kBlockO != 0 || K % kBlockK != 0 || x_ld % 8 != 0 || ld_out % 8 != 0 || m_cap < 1)
+  if (O % kBlockO != 0 || K % kBlockK != 0 || x_ld % 8 != 0 || ld_out % 8 != 0 || m_cap < 1 ||
+      w_kind < kWBf16 || w_kind > kWF16)
     return -3;
+  const bool w_int8 = w_kind == kWInt8;
   plan->O = O;
   plan->K = K;
-  plan->w_int8 = w_int8;
+  plan->w_kind = w_kind;
   plan->m_cap = m_cap;
   plan->tn = gemm_token_tile(O, m_cap, sm_count());
   plan->out_mode = out_mode;
@@ -559,7 +603,7 @@ int gemm_prepare(GemmPlan* plan, const void* w, bool w_int8, int O, int K, const
                             false);
   } else {
     rc = make_tensor_map_2d(&plan->tm_w, w, 2, K, O, static_cast<uint64_t>(K) * 2, kBlockK,
-                            kBlockO, true);
+                            kBlockO, true, w_kind == kWF16);
   }
   if (rc) return rc;
   // The activation map covers exactly m_cap rows (TMA zero-fills rows past it).
@@ -568,10 +612,10 @@ int gemm_prepare(GemmPlan* plan, const void* w, bool w_int8, int O, int K, const
   // then hold stale data that only reaches output columns t >= m_cap, which
   // the epilogue never stores (it stops at the live token count M <= m_cap).
   plan->x_box_rows = m_cap < plan->tn ? m_cap : plan->tn;
-  // activations are fp16 when the weights are int8, bf16 otherwise
+  // activations are fp16 when the weights are int8 (either kind), bf16 otherwise
   rc = make_tensor_map_2d(&plan->tm_x, x, 2, K, static_cast<uint64_t>(m_cap),
                           static_cast<uint64_t>(x_ld) * 2, kBlockK,
-                          static_cast<uint32_t>(plan->x_box_rows), true, w_int8);
+                          static_cast<uint32_t>(plan->x_box_rows), true, w_kind != kWBf16);
   if (rc) return rc;
   // The output [m_cap rows][ld_out] is written with plain stores, clipped at
   // the live token count, so it needs no tensor map.
@@ -595,8 +639,9 @@ cudaError_t gemm_launch(const GemmPlan& plan, GemmParams p, int splits, cudaStre
   const int sms = sm_count();
 #define LB_GEMM_CASE(TNV)                                                                  \
   case TNV:                                                                                \
-    return plan.w_int8 ? launch_gemm_t<TNV, true>(plan, p, splits, sms, stream)            \
-                       : launch_gemm_t<TNV, false>(plan, p, splits, sms, stream);
+    return plan.w_kind == kWInt8  ? launch_gemm_t<TNV, kWInt8>(plan, p, splits, sms, stream) \
+           : plan.w_kind == kWF16 ? launch_gemm_t<TNV, kWF16>(plan, p, splits, sms, stream)  \
+                                  : launch_gemm_t<TNV, kWBf16>(plan, p, splits, sms, stream);
   switch (plan.tn) {
     LB_GEMM_CASE(32)
     LB_GEMM_CASE(64)

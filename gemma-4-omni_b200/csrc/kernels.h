@@ -39,7 +39,7 @@ struct GemmPlan {
   int x_box_rows = 0;    // rows per activation TMA box: min(tn, m_cap)
   int out_mode = 0;
   bool out_f16 = false;
-  bool w_int8 = false;
+  int w_kind = 0;  // 0 bf16 weights, 1 int8 codes (widened in-kernel), 2 fp16 codes of int8
 };
 
 int make_tensor_map_2d(CUtensorMap* map, const void* base, int elem_bytes, uint64_t inner,
@@ -48,12 +48,15 @@ int make_tensor_map_2d(CUtensorMap* map, const void* base, int elem_bytes, uint6
 // Token tile (UMMA N) for an [m_cap x O] output: 32/64/128/256 up to 256
 // tokens, beyond that the multiple of 16 in [128, 256] that fills whole waves.
 int gemm_token_tile(int O, int m_cap, int num_sms);
-// Encodes the tensor maps for W ([O,K] bf16 or int8), X ([m_cap,K], row stride
-// x_ld elements; bf16, or fp16 when W is int8; TMA zero-fills rows past m_cap)
-// and the output ([m_cap, ld_out]: out_mode 0 bf16 or, with out_f16, fp16;
-// fp32 otherwise; stores past m_cap are clipped).
-int gemm_prepare(GemmPlan* plan, const void* w, bool w_int8, int O, int K, const void* x, int x_ld,
+// Encodes the tensor maps for W ([O,K]: bf16, int8 codes or fp16 codes of int8,
+// per w_kind) and X ([m_cap,K], row stride x_ld elements; bf16, or fp16 with
+// either int8 kind; TMA zero-fills rows past m_cap).  The output [m_cap, ld_out]
+// is out_mode 0 bf16 (fp16 with out_f16), else fp32; rows past the live token
+// count are never written.
+int gemm_prepare(GemmPlan* plan, const void* w, int w_kind, int O, int K, const void* x, int x_ld,
                  int m_cap, void* out, int ld_out, int out_mode, bool out_f16 = false);
+// dst[i] = fp16(src[i]) for n int8 codes (n % 16 == 0, 16-byte aligned).
+cudaError_t widen_int8_codes(const void* src, void* dst, size_t n, cudaStream_t stream);
 cudaError_t gemm_launch(const GemmPlan& plan, GemmParams p, int splits, cudaStream_t stream);
 // K-split count that fills the SMs for an [m_cap x O] output with K reduction.
 int gemm_pick_splits(int O, int K, int m_cap, int num_sms);

@@ -3,7 +3,10 @@
 // Device memory layout (all owned by the context, allocated at lb_create):
 //
 //   weights   one arena; GEMM weights bf16 [O,K] or int8 [O,K] + fp16 scale[O];
-//             norms / conv / biases fp32 (bf16-rounded values).
+//             norms / conv / biases fp32 (bf16-rounded values).  With int8
+//             weights and buckets of >= 512 tokens, a second arena holds the
+//             int8 codes widened to fp16 (exact): those GEMMs are tensor-bound,
+//             and fp16 codes skip the in-kernel widening.
 //   sessions  persistent per-slot state, S = max_sessions slots:
 //               kv_k, kv_v  bf16 [S][L][16][d]   ring of the last 13 projected
 //                           keys / values (pre-scale, exactly the bf16 linear
@@ -126,6 +129,10 @@ struct Ctx {
   // arenas
   void* weight_arena = nullptr;
   size_t weight_bytes = 0;
+  // int8 weights: the whole weight arena widened byte-for-byte to fp16, so the
+  // fp16 codes of an int8 tensor at arena offset b sit at byte offset 2b here
+  // (null when not built).  Large buckets read these instead of the int8 codes.
+  void* wide_arena = nullptr;
   void* state_arena = nullptr;
   size_t state_bytes = 0;
   void* act_arena = nullptr;

@@ -108,7 +108,10 @@ int lb_destroy(lb_ctx* ctx);
  * "layers.<i>.self_attn.query_scale" [head_dim] f32).  GEMM weights are LB_BF16,
  * or LB_I8 with a companion "<name>:scale" LB_F16 [rows] tensor.  Synchronous. */
 int lb_set_tensor(lb_ctx* ctx, const char* name, const void* host_data, int dtype, int64_t numel);
-/* Checks that every required parameter was uploaded.  Must precede stepping. */
+/* Checks that every required parameter was uploaded.  Must precede stepping,
+ * and follow any later lb_set_tensor (which un-finalizes the context).  With
+ * int8 weights and max_rows >= 256 it also builds the fp16-widened copy of
+ * the int8 codes that buckets of >= 512 tokens read (synchronous). */
 int lb_finalize_weights(lb_ctx* ctx);
 /* Number of parameter names the context expects, and the i-th name. */
 int lb_tensor_count(lb_ctx* ctx);
@@ -192,10 +195,12 @@ int lb_debug_read_buffer(lb_ctx* ctx, const char* name, void* host_dst, size_t b
 /* D[t,o] = sum_k X[t,k] W[o,k] (+bias[o]) on tcgen05 tensor cores.
  * Replaces Gemma4ClippableLinear.forward / the reference Triton clipped
  * linear (duplex_kernel/streaming_conformer_kernels.py:27-76, 110-168).
- * w: bf16 [out_features, k], or int8 with w_scale fp16 [out_features];
- * x: [m, x_ld] (K-contiguous, x_ld % 8 == 0), bf16 with bf16 weights and
- * fp16 with int8 weights (the int8 codes widen exactly to fp16 and the
- * product runs as an fp16 x fp16 MMA); out_mode 0 = bf16, 1 = fp32,
+ * w_int8 selects the weight format of w [out_features, k]: 0 = bf16;
+ * 1 = int8 codes, widened to fp16 inside the kernel; 2 = the same codes
+ * already widened to fp16 (exact), read directly.  With 1 or 2, w_scale is
+ * the fp16 per-output-channel scale and x is fp16 (the product runs as an
+ * fp16 x fp16 MMA); with 0, x is bf16.  x: [m, x_ld] (K-contiguous,
+ * x_ld % 8 == 0); out_mode 0 = bf16, 1 = fp32,
  * 2 = fp32 atomic accumulate (caller zeroes out; required when splits > 1);
  * act 1 = SiLU of the bf16-rounded product (bf16 output only).
  * out_features % 128 == 0, k % 64 == 0. */

@@ -19,12 +19,14 @@ pytestmark = pytest.mark.gpu
 LB_ERR_CAPACITY = -4
 SCRATCH_FLOATS = 1 << 21
 
-# (m, out_features, k, int8 weights, act, splits, bias, extra output columns)
+# (m, out_features, k, weight kind, act, splits, bias, extra output columns);
+# weight kind 0 = bf16, 1 = int8 codes, 2 = int8 codes widened to fp16
 CASES = [
-    (64, 1536, 6144, True, 0, 4, True, 0),
-    (200, 6144, 1536, False, 1, 2, True, 128),
-    (1, 1536, 1536, True, 1, 3, False, 0),
-    (130, 2048, 3072, False, 0, 1, False, 0),
+    (64, 1536, 6144, 1, 0, 4, True, 0),
+    (200, 6144, 1536, 0, 1, 2, True, 128),
+    (1, 1536, 1536, 1, 1, 3, False, 0),
+    (130, 2048, 3072, 0, 0, 1, False, 0),
+    (96, 1536, 3072, 2, 1, 2, True, 0),
 ]
 
 
@@ -34,6 +36,8 @@ def _operands(m, o, k, int8, bias, seed):
     x = (torch.randn(m, k, generator=g) * 0.5).to(torch.float16 if int8 else torch.bfloat16).to(dev)
     if int8:
         w = torch.randint(-127, 128, (o, k), generator=g, dtype=torch.int8).to(dev)
+        if int8 == 2:
+            w = w.to(torch.float16)
         sc = (torch.rand(o, generator=g) * 1e-3 + 1e-4).to(torch.float16).to(dev)
     else:
         w = (torch.randn(o, k, generator=g) * 0.02).to(torch.bfloat16).to(dev)
