@@ -191,6 +191,9 @@ class Schedule:
         self.rows = []
         for _ in range(steps):
             lanes, sids, frames, new = ar.step()
+            # global session ids gid = id_offset (mod id_stride): with offset = rank
+            # and stride = world these are exactly the ids sharding.shard_of
+            # routes to this rank
             gids = sids * id_stride + id_offset
             alive = set(gids.tolist())
             released = [h for g, h in list(live.items()) if g not in alive]
@@ -416,12 +419,10 @@ def main():
     elapsed_ms, e2e_s = res["elapsed_ms"], res["e2e_s"]
     frames, e2e_frames = res["frames"], res["e2e_frames"]
     if world > 1:
-        t = torch.tensor([elapsed_ms, e2e_s], dtype=torch.float64, device=device)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        elapsed_ms, e2e_s = t.tolist()
-        c = torch.tensor([frames, e2e_frames], dtype=torch.float64, device=device)
-        torch.distributed.all_reduce(c, op=torch.distributed.ReduceOp.SUM)
-        frames, e2e_frames = (int(v) for v in c.tolist())
+        from gemma4_omni_b200 import sharding
+        # whole job: the slowest rank's time, every rank's frames
+        (elapsed_ms, e2e_s), (frames, e2e_frames) = sharding.reduce_over_ranks(
+            [elapsed_ms, e2e_s], [frames, e2e_frames], device=device)
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
     if rank != 0:

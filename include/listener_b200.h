@@ -208,6 +208,41 @@ int lb_op_gemm(const void* x, int x_ld, int m, const void* w, int w_int8, const 
                const float* bias, int out_features, int k, void* out, int ld_out, int out_mode,
                int act, int splits, int* status_dev, void* stream);
 
+/* ----------------------------------------------------------------------
+ * Tick-level row selection (device arrays, asynchronous on `stream`).
+ * ---------------------------------------------------------------------- */
+
+/* One tick's rows over n_registered sessions in registration order.
+ * Replaces SharedListenerTickDispatcher._snapshot_ready_rows
+ * (duplex_kernel/shared_listener_scheduler.py:486-535): paused sessions are
+ * skipped; a session's deferred frame is taken before its ingress head; a frame
+ * enqueued after deadline_ns becomes (or stays) the deferred frame; every
+ * other frame is a row.  Per session: paused, deferred_valid/_frame_id/
+ * _enqueue_ns (updated in place), head_valid/_frame_id/_enqueue_ns (the
+ * ingress queue head).  Outputs: rows_out[k] = registration index of row k
+ * (registration order), row_frame_id_out[k], popped_out[i] = 1 when session
+ * i's ingress head was consumed (the host pops it), *n_rows_out. */
+int lb_snapshot_ready_rows(int n_registered, const uint8_t* paused, uint8_t* deferred_valid,
+                           int64_t* deferred_frame_id, int64_t* deferred_enqueue_ns,
+                           const uint8_t* head_valid, const int64_t* head_frame_id,
+                           const int64_t* head_enqueue_ns, int64_t deadline_ns, int32_t* rows_out,
+                           int64_t* row_frame_id_out, uint8_t* popped_out, int32_t* n_rows_out,
+                           void* stream);
+
+/* Dispatch order of the candidate heads (queue heads of sessions not in
+ * flight).  Replaces ListenerMicrobatchCoordinator._candidate_heads_locked /
+ * _take_ready_locked (duplex_kernel/listener_microbatch.py:170-201): heads with
+ * ready_at_ns <= now_ns sorted by (ready_at_ns, submission_order, session id),
+ * session_rank being the rank of the session id in string order; a single
+ * ready head waits until ready_at + coalesce_ns.  Outputs perm_out[0..count)
+ * (indices into the inputs), *count_out (0 = nothing dispatched) and
+ * *reason_out: 0 none, 1 batch_full (count == n_registered), 2 multiple_ready,
+ * 3 coalesce_deadline.  n_heads <= 8192 (else LB_ERR_CAPACITY). */
+int lb_order_ready_heads(int n_heads, const int64_t* ready_at_ns, const int64_t* submission_order,
+                         const int32_t* session_rank, int64_t now_ns, int64_t coalesce_ns,
+                         int n_registered, int32_t* perm_out, int32_t* count_out, int32_t* reason_out,
+                         void* stream);
+
 /* lb_op_gemm's split-K form with a bf16 output [m, ld_out] and no
  * caller-supplied accumulator: the fp32 partial sums of the `splits` K slices
  * are reduce-added into a fixed device array inside the library (8 MiB, i.e.
