@@ -437,11 +437,13 @@ def main():
     gemm_flops = 2.0 * M * FULL.ffn * FULL.hidden
     achieved = gemm_flops / (res["gemm_ms"] * 1e-3) / 1e12
     # DRAM bytes (read + write) of one launch of this GEMM from an ncu --set full
-    # capture of the same shape (M=2048, int8 weights, fp16 activations): W and X
-    # are read once (15.79 MB); the 25 MB output stays in L2 by kernel end.
+    # capture of the same shape and weight kind (M=2048, fp16 activations): W and
+    # X are read once; the 25 MB output stays in L2 by kernel end.
     traffic, traffic_src = None, None
-    if M == 2048 and args.weights == "int8" and res["w_kind"] == 1:
-        traffic, traffic_src = 15.794432e6, "ncu dram__bytes_read.sum + dram__bytes_write.sum, bytes per launch"
+    if M == 2048 and args.weights == "int8":
+        # in-kernel widening reads 9.4 MB of int8 codes, fp16 codes 18.9 MB (+ 6.3 MB X)
+        traffic = {1: 15.794432e6, 2: 25.478144e6}.get(res["w_kind"])
+        traffic_src = "ncu dram__bytes_read.sum + dram__bytes_write.sum, bytes per launch"
     # whole-step roofline (BASELINE: F = N x 2.644 GFLOP, B = W + N x 1.24 MB)
     n = args.sessions
     W = 0.659e9 if args.weights == "int8" else 1.318e9
