@@ -288,9 +288,9 @@ size_t layout_state(Ctx& c, char* base) {
   const size_t R = g.max_rows, T = 2 * R;
   Arena a;
   a.base = base;
-  auto kk = a.take<__nv_bfloat16>(S * L * kRing * d, 4096);
-  auto vv = a.take<__nv_bfloat16>(S * L * kRing * d, 4096);
-  auto cr = a.take<__nv_bfloat16>(S * L * kConvRing * d, 4096);
+  auto kk = a.take<__nv_bfloat16>(S * L * (kRing * d + kRingPad), 4096);
+  auto vv = a.take<__nv_bfloat16>(S * L * (kRing * d + kRingPad), 4096);
+  auto cr = a.take<__nv_bfloat16>(S * L * (kConvRing * d + kRingPad), 4096);
   auto sp = a.take<__nv_bfloat16>(S * 2 * 64 * 128);
   auto mp = a.take<float>(S * 2 * kMelBins);
   auto pt = a.take<float>(S * 2 * kTail);
@@ -727,6 +727,7 @@ int lb_destroy(lb_ctx* x) {
   if (x->pinned) cudaFreeHost(x->pinned);
   cudaFree(c.weight_arena);
   if (c.wide_arena) cudaFree(c.wide_arena);
+  if (c.rel_bf16_arena) cudaFree(c.rel_bf16_arena);
   cudaFree(c.state_arena);
   cudaFree(c.act_arena);
   delete x;
@@ -824,6 +825,14 @@ int lb_finalize_weights(lb_ctx* x) {
       c.w.layers[i].clip[kLinQkv][k] = b;
     }
   }
+  cudaSetDevice(c.device);
+  if (!c.rel_bf16_arena &&
+      cudaMalloc(&c.rel_bf16_arena, static_cast<size_t>(c.cfg.layers) * 13 * c.cfg.hidden * 2) != cudaSuccess) {
+    c.rel_bf16_arena = nullptr;
+    return LB_ERR_CUDA;
+  }
+  if (attention_prepare(c, nullptr) != cudaSuccess || cudaStreamSynchronize(nullptr) != cudaSuccess)
+    return LB_ERR_CUDA;
   const char* env = std::getenv("LB_INT8_WIDE");
   if (c.weight_int8 && 2 * c.cfg.max_rows >= kWideMinTokens && !(env && env[0] == '0')) {
     {

@@ -47,6 +47,24 @@ __device__ __forceinline__ void store8(float* p, const float (&v)[8]) {
   reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
   reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
 }
+// Read-only (non-coherent) forms for data the kernel never writes: the
+// compiler may then issue them ahead of the kernel's own stores.
+__device__ __forceinline__ void load8_nc(const float* p, float (&v)[8]) {
+  const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+  const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+__device__ __forceinline__ void load8_bf16_nc(const __nv_bfloat16* p, float (&v)[8]) {
+  const int4 r = __ldg(reinterpret_cast<const int4*>(p));
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&r);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
 __device__ __forceinline__ void load8_bf16(const __nv_bfloat16* p, float (&v)[8]) {
   const int4 r = *reinterpret_cast<const int4*>(p);
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&r);
@@ -63,6 +81,17 @@ __device__ __forceinline__ void store8_bf16(__nv_bfloat16* p, const float (&v)[8
 #pragma unroll
   for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
   *reinterpret_cast<int4*>(p) = r;
+}
+
+// RMSNorm with the weights already in registers (w8: this thread's 8 weights).
+__device__ __forceinline__ void rms8w(float (&v)[8], const float (&w8)[8], int d, float eps, float* sh) {
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) ss += v[i] * v[i];
+  ss = block_sum(ss, sh);
+  const float r = rsqrtf(ss / static_cast<float>(d) + eps);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = v[i] * r * w8[i];
 }
 
 // RMSNorm of 8-element thread slices over a block row: x * pow(mean(x^2)+eps, -0.5) * w
@@ -109,15 +138,21 @@ __global__ void __launch_bounds__(256) row_fused_kernel(RowFusedDev a) {
   if (t >= a.counts[1]) return;
   const int e0 = threadIdx.x * 8;
   const size_t base = static_cast<size_t>(t) * a.d + e0;
-  float hv[8];
+  // every input is requested up front: the row, the GEMM output and the (read
+  // only) norm weights, so the row costs one memory round trip before its stores
+  float hv[8], yv[8], pw[8], ow[8], qw[8];
   load8(a.h + base, hv);
+  if (a.y) load8(a.y + base, yv);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) pw[i] = ow[i] = qw[i] = 1.0f;
+  if (a.post_w) load8_nc(a.post_w + e0, pw);
+  if (a.out_w) load8_nc(a.out_w + e0, ow);
+  if (a.xa && a.pre_norm && a.pre_w) load8_nc(a.pre_w + e0, qw);
   if (a.y) {
-    float yv[8];
-    load8(a.y + base, yv);
     if (a.post_w) {
 #pragma unroll
       for (int i = 0; i < 8; ++i) yv[i] = fminf(fmaxf(yv[i], -a.clip), a.clip);
-      rms8(yv, a.post_w, e0, a.d, a.eps, sh);
+      rms8w(yv, pw, a.d, a.eps, sh);
     }
 #pragma unroll
     for (int i = 0; i < 8; ++i) hv[i] = a.residual ? fmaf(yv[i], a.alpha, hv[i]) : yv[i] * a.alpha;
@@ -125,7 +160,7 @@ __global__ void __launch_bounds__(256) row_fused_kernel(RowFusedDev a) {
   if (a.out_w) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) hv[i] = fminf(fmaxf(hv[i], -a.clip), a.clip);
-    rms8(hv, a.out_w, e0, a.d, a.eps, sh);
+    rms8w(hv, ow, a.d, a.eps, sh);
   }
   store8(a.h + base, hv);
   if (a.dbg) store8(a.dbg + base, hv);
@@ -133,7 +168,7 @@ __global__ void __launch_bounds__(256) row_fused_kernel(RowFusedDev a) {
     float xv[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) xv[i] = a.pre_clamp ? fminf(fmaxf(hv[i], -a.clip), a.clip) : hv[i];
-    if (a.pre_norm) rms8(xv, a.pre_w, e0, a.d, a.eps, sh);
+    if (a.pre_norm) rms8w(xv, qw, a.d, a.eps, sh);
 #pragma unroll
     for (int i = 0; i < 8; ++i) xv[i] = fminf(fmaxf(xv[i], a.in_lo), a.in_hi);
     store8_act(a.xa + base, xv, a.f16);
@@ -150,7 +185,7 @@ struct LconvDev {
   const float* dw;           // [5][d] tap-major
   const float* norm_w;       // [d]
   __nv_bfloat16* xa;         // [tok][d]
-  int layer, layers, d;
+  int layer, layers, d, slots;
   float eps, clip, in_lo, in_hi;
   bool f16;  // xa holds fp16 (int8-weight GEMM input) instead of bf16
 };
@@ -166,7 +201,7 @@ __global__ void __launch_bounds__(128) lconv_kernel(LconvDev a) {
   const int d = G * 256;
   const int slot = a.row_slot[row];
   const SlotMeta m = a.row_meta[row];
-  const size_t rb = (static_cast<size_t>(slot) * a.layers + a.layer) * kConvRing * d;
+  const size_t rb = ring_base(slot, a.layer, a.slots, kConvRing, d);
   const int first_real = 4 - min(m.fill, 4);  // ring rows written since the last reset
   float cv[2][G][8];
   float ss0 = 0.f, ss1 = 0.f;
@@ -176,8 +211,8 @@ __global__ void __launch_bounds__(128) lconv_kernel(LconvDev a) {
     float win[6][8];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      if (j >= first_real) {
-        load8_bf16(a.ring + rb + static_cast<size_t>((m.pos + j) & (kConvRing - 1)) * d + e0, win[j]);
+      if (j >= first_real) {  // canonical rows: read-only here (the step writes only staged rows)
+        load8_bf16_nc(a.ring + rb + static_cast<size_t>((m.pos + j) & (kConvRing - 1)) * d + e0, win[j]);
       } else {
 #pragma unroll
         for (int i = 0; i < 8; ++i) win[j][i] = 0.f;
@@ -187,15 +222,15 @@ __global__ void __launch_bounds__(128) lconv_kernel(LconvDev a) {
     for (int t = 0; t < 2; ++t) {
       float av[8], bv[8];
       const __nv_bfloat16* gp = a.gl + (static_cast<size_t>(row) * 2 + t) * 2 * d;
-      load8_bf16(gp + e0, av);
-      load8_bf16(gp + d + e0, bv);
+      load8_bf16_nc(gp + e0, av);
+      load8_bf16_nc(gp + d + e0, bv);
 #pragma unroll
       for (int i = 0; i < 8; ++i) win[4 + t][i] = bf16_round(__fdividef(av[i], 1.0f + __expf(-bv[i])));  // GLU
       store8_bf16(a.ring + rb + static_cast<size_t>((m.pos + 4 + t) & (kConvRing - 1)) * d + e0, win[4 + t]);
     }
     float w5t[5][8];  // tap-major weights: 2 vector loads per tap
 #pragma unroll
-    for (int k = 0; k < 5; ++k) load8(a.dw + static_cast<size_t>(k) * d + e0, w5t[k]);
+    for (int k = 0; k < 5; ++k) load8_nc(a.dw + static_cast<size_t>(k) * d + e0, w5t[k]);
 #pragma unroll
     for (int t = 0; t < 2; ++t)
 #pragma unroll
@@ -215,7 +250,7 @@ __global__ void __launch_bounds__(128) lconv_kernel(LconvDev a) {
   for (int g = 0; g < G; ++g) {
     const int e0 = (g * 32 + lane) * 8;
     float wv[8];
-    load8(a.norm_w + e0, wv);
+    load8_nc(a.norm_w + e0, wv);
 #pragma unroll
     for (int t = 0; t < 2; ++t) {
       float o[8];
@@ -375,6 +410,7 @@ cudaError_t launch_lconv(Ctx& c, int layer, int rows_cap, cudaStream_t s) {
   a.layer = layer;
   a.layers = c.cfg.layers;
   a.d = c.cfg.hidden;
+  a.slots = c.cfg.max_sessions;
   a.eps = c.cfg.rms_eps;
   a.clip = c.cfg.gradient_clipping;
   a.in_lo = c.w.layers[layer].clip[7][0];  // linear_end input bounds

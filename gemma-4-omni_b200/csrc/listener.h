@@ -8,10 +8,10 @@
 //             int8 codes widened to fp16 (exact): those GEMMs are tensor-bound,
 //             and fp16 codes skip the in-kernel widening.
 //   sessions  persistent per-slot state, S = max_sessions slots:
-//               kv_k, kv_v  bf16 [S][L][16][d]   ring of the last 13 projected
-//                           keys / values (pre-scale, exactly the bf16 linear
-//                           outputs) plus 2 staged + 1 spare entries
-//               conv_ring   bf16 [S][L][8][d]    ring of the last 4 GLU rows + 2 staged
+//               kv_k, kv_v  bf16 [L][S][16][d] (+pad per slot, ring_base) ring of the
+//                           last 13 projected keys / values (pre-scale, exactly
+//                           the bf16 linear outputs) plus 2 staged + 1 spare
+//               conv_ring   bf16 [L][S][8][d] (+pad)  last 4 GLU rows + 2 staged
 //               sub_prev    bf16 [S][2][128][64] last conv0 output row, double-buffered
 //               mel_prev    f32  [S][2][128]     last mel row, double-buffered
 //               pcm_tail    f32  [S][2][160]     last 160 PCM samples, double-buffered
@@ -46,6 +46,17 @@ constexpr int kMelBins = 128;
 constexpr int kPcm = 1280;
 constexpr int kTail = 160;
 
+// Ring storage is layer-major: for each layer, the slots' rings follow one
+// another at a stride of (entries * d + kRingPad) elements.  Concurrent CTAs
+// (one per session) read the same layer and ring entry of different slots; the
+// 128-byte pad keeps those rows from sharing the low address bits that a
+// power-of-two-multiple stride would give them, which spreads them over the
+// DRAM channels.
+constexpr int kRingPad = 64;  // bf16 elements
+__host__ __device__ inline size_t ring_base(int slot, int layer, int slots, int entries, int d) {
+  return (static_cast<size_t>(layer) * slots + slot) * (static_cast<size_t>(entries) * d + kRingPad);
+}
+
 struct SlotMeta {
   int pos;         // ring base: canonical entries are (pos + j) mod ring
   int fill;        // tokens written since the last reset (saturates at 13)
@@ -64,6 +75,7 @@ struct LayerW {
   __half* s_post;
   float* q_mult;    // [hd] q_scale * softplus(per_dim_scale)
   float* rel_keys;  // [13][d] relative keys, fp32
+  __nv_bfloat16* rel_bf16;  // [13][d] the same, bf16 (attention MMA operand; set at finalize)
   float *lc_pre, *lc_norm;
   float* lc_dw;     // [5][d] tap-major (transposed from [d][1][5] on upload)
   void *w_lstart, *w_lend;
@@ -133,6 +145,7 @@ struct Ctx {
   // fp16 codes of an int8 tensor at arena offset b sit at byte offset 2b here
   // (null when not built).  Large buckets read these instead of the int8 codes.
   void* wide_arena = nullptr;
+  __nv_bfloat16* rel_bf16_arena = nullptr;  // [L][13][d] bf16 relative keys
   void* state_arena = nullptr;
   size_t state_bytes = 0;
   void* act_arena = nullptr;
@@ -236,6 +249,8 @@ struct RowFusedArgs {
 };
 cudaError_t launch_row_fused(Ctx& c, int tok_cap, const RowFusedArgs& a, cudaStream_t s);
 cudaError_t launch_attention(Ctx& c, int layer, int rows_cap, cudaStream_t s);
+// bf16 copies of every layer's relative keys (after the weights are uploaded).
+cudaError_t attention_prepare(Ctx& c, cudaStream_t s);
 cudaError_t launch_lconv(Ctx& c, int layer, int rows_cap, cudaStream_t s);
 cudaError_t launch_finalize_wide(Ctx& c, int tok_cap, const float* acc, int width, int act,
                                  __nv_bfloat16* out, const float* out_clip, bool out_f16, cudaStream_t s);
