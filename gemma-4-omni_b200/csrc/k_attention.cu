@@ -104,15 +104,19 @@ __global__ void __launch_bounds__(512) attention_kernel(AttnDev a) {
   constexpr int KS = HD / 16;  // MMA k-steps over the head dimension
   extern __shared__ __align__(128) unsigned char smem_att[];
   const int row = blockIdx.x;
-  if (row >= a.counts[0]) return;
+  // the row tables are read together with the live row count (one round trip);
+  // they are in bounds for every row of the bucket, and a row past the count
+  // uses none of them
+  const int n_rows = a.counts[0];
+  const int slot = a.row_slot[row];
+  const SlotMeta m = a.row_meta[row];
+  const int mask = a.row_mask[row];
+  if (row >= n_rows) return;
   const int head = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;  // MMA fragment coordinates
   unsigned char* ws = smem_att + head * L::kBytes;
   uint64_t* bar = reinterpret_cast<uint64_t*>(ws + L::kBar);
   float* sl = reinterpret_cast<float*>(ws + L::kLogit);
-  const int slot = a.row_slot[row];
-  const SlotMeta m = a.row_meta[row];
-  const int mask = a.row_mask[row];
   const int d = a.d;
   const size_t ring_off = ring_base(slot, a.layer, a.slots, kRing, d);
   const int hoff = head * HD;

@@ -40,14 +40,17 @@ struct MelArgs {
 
 __global__ void __launch_bounds__(256) mel_kernel(MelArgs a) {
   const int row = blockIdx.x;
-  if (row >= a.counts[0]) return;
   __shared__ float x[kFrames * kWin];
   __shared__ float mag[kFrames][kBins + 3];
   __shared__ float ct[512], st[512];
+  // row tables (in bounds for every row of the bucket) read with the live count
+  const int n_rows = a.counts[0];
   const int slot = a.row_slot[row];
   const int parity = (a.row_meta[row].pos >> 1) & 1;
+  const int reason = a.row_reason[row];
+  if (row >= n_rows) return;
   // identity resets start a fresh session: no previous PCM tail
-  const bool fresh = a.row_reason[row] == 3 || a.row_reason[row] == 1;
+  const bool fresh = reason == 3 || reason == 1;
   const float* tail_in = a.tail + (static_cast<size_t>(slot) * 2 + parity) * kTail;
   const float* pcm = a.pcm + static_cast<size_t>(row) * kPcm;
   for (int i = threadIdx.x; i < 512; i += blockDim.x) {
@@ -133,6 +136,20 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+__device__ __forceinline__ void mma_f16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                              uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_f16x2(float x, float y) {
+  const __half2 h = __floats2half2_rn(x, y);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
 // C1 = 32 output channels (validated at create): 8 warps = 4 position tiles x 2 channel halves.
 __global__ void __launch_bounds__(kSubThreads, 1) subsample_kernel(SubArgs a) {
   extern __shared__ uint8_t smem_raw[];
@@ -140,7 +157,7 @@ __global__ void __launch_bounds__(kSubThreads, 1) subsample_kernel(SubArgs a) {
                                            ~static_cast<uintptr_t>(127));
   __nv_bfloat16* w1s = reinterpret_cast<__nv_bfloat16*>(sp);           // [32][kK1Pad]
   __nv_bfloat16* xin = w1s + 32 * kK1Pad;                              // [5][66][kCiPad]
-  float* w0s = reinterpret_cast<float*>(xin + 5 * 66 * kCiPad);        // [128][12] (9 taps + pad)
+  float* w0s = reinterpret_cast<float*>(xin + 5 * 66 * kCiPad);        // [128][12] (unused)
   float* ln0s = w0s + 128 * 12;                                        // [128]
   float* mels = ln0s + 128;                                            // [9][130]
   float* c1out = mels + 9 * 130;                                       // [64][33]
@@ -148,12 +165,24 @@ __global__ void __launch_bounds__(kSubThreads, 1) subsample_kernel(SubArgs a) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   for (int i = tid; i < 32 * kK1Pad / 8; i += blockDim.x)
     reinterpret_cast<int4*>(w1s)[i] = reinterpret_cast<const int4*>(a.w1)[i];
-  for (int i = tid; i < 128 * 12; i += blockDim.x) w0s[i] = (i % 12) < 9 ? a.w0[(i / 12) * 9 + i % 12] : 0.f;
   for (int i = tid; i < 128; i += blockDim.x) ln0s[i] = a.ln0[i];
   // zero the frequency padding columns of the conv1 input once (never written)
   for (int i = tid; i < 5 * 2 * kCiPad; i += blockDim.x) {
     const int r = i / (2 * kCiPad), side = (i / kCiPad) & 1, c = i % kCiPad;
     xin[(r * 66 + (side ? 65 : 0)) * kCiPad + c] = __float2bfloat16_rn(0.0f);
+  }
+  // conv0 weights as m16n8k16 B fragments (taps 9..15 zero), held for every row:
+  // n-tile nt covers channels nt*8 .. +7; this lane's column is channel nt*8 + g
+  uint32_t w0b[16][2];
+  {
+    const int g = lane >> 2, tq = lane & 3;
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt) {
+      const float* wr = a.w0 + (nt * 8 + g) * 9;
+      auto tap = [&](int k) { return k < 9 ? wr[k] : 0.0f; };
+      w0b[nt][0] = pack_f16x2(tap(2 * tq), tap(2 * tq + 1));
+      w0b[nt][1] = pack_f16x2(tap(2 * tq + 8), tap(2 * tq + 9));
+    }
   }
   const int n_rows = a.counts[0];
   for (int row = blockIdx.x; row < n_rows; row += gridDim.x) {
@@ -192,50 +221,75 @@ __global__ void __launch_bounds__(kSubThreads, 1) subsample_kernel(SubArgs a) {
     __syncthreads();
     // staged mel_prev = last mel row (unmasked)
     for (int i = tid; i < kMelBins; i += blockDim.x) mp_out[i] = mel_in[7 * kMelBins + i];
-    // ---- conv0 + LN(128) + ReLU: thread -> one of the 4 x 64 output positions,
-    // its 3x3 input window in registers; the 9-tap channel outputs are cheap, so
-    // they are recomputed in each of the three passes (mean, centred variance,
-    // output) instead of being held: no cross-thread reduction, no spill.
+    // ---- conv0 + LN(128) + ReLU on the tensor cores: D[pos][ch] = sum_tap A[pos][tap] W0[ch][tap]
+    // as one m16n8k16 per (16 positions, 8 channels) -- the 9 taps padded to 16,
+    // fp16 operands (the mel rounded to fp16; the bf16-valued weights exactly),
+    // fp32 accumulation.  Warp w owns time row t = w/2 and frequencies
+    // (w&1)*32 .. +31 (two 16-position m-tiles); each position's 128 channels
+    // sit in one lane quad, so the LayerNorm statistics are two quad shuffles.
     __nv_bfloat16* sp_out = a.sub_prev + (static_cast<size_t>(slot) * 2 + (parity ^ 1)) * kF0 * 128;
     {
-      const int t = tid >> 6, fq = tid & 63;
-      float xw[9];
-#pragma unroll
-      for (int i = 0; i < 3; ++i)
-#pragma unroll
-        for (int j = 0; j < 3; ++j) xw[i * 3 + j] = mels[(2 * t + i) * 130 + 2 * fq + j];  // padded freq + 1
-      auto chan = [&](int c) {
-        const float4 w0 = *reinterpret_cast<const float4*>(w0s + c * 12);
-        const float4 w1 = *reinterpret_cast<const float4*>(w0s + c * 12 + 4);
-        float v = w0.x * xw[0];
-        v = fmaf(w0.y, xw[1], v);
-        v = fmaf(w0.z, xw[2], v);
-        v = fmaf(w0.w, xw[3], v);
-        v = fmaf(w1.x, xw[4], v);
-        v = fmaf(w1.y, xw[5], v);
-        v = fmaf(w1.z, xw[6], v);
-        v = fmaf(w1.w, xw[7], v);
-        return fmaf(w0s[c * 12 + 8], xw[8], v);
-      };
-      float sum = 0.f;
-#pragma unroll 8
-      for (int c = 0; c < 128; ++c) sum += chan(c);
-      const float mean = sum * (1.0f / 128.0f);
-      float var = 0.f;
-#pragma unroll 8
-      for (int c = 0; c < 128; ++c) {
-        const float dv = chan(c) - mean;
-        var = fmaf(dv, dv, var);
-      }
-      const float rstd = rsqrtf(var * (1.0f / 128.0f) + a.eps);
+      const int t = warp >> 1;
+      const int g = lane >> 2, tq = lane & 3;
       const bool keep = (mask >> (2 * t)) & 1;  // mask0 = mask[::2]
-      __nv_bfloat16* xdst = xin + ((1 + t) * 66 + fq + 1) * kCiPad;
-#pragma unroll 4
-      for (int c = 0; c < 128; c += 2) {
-        const __nv_bfloat162 o = __floats2bfloat162_rn(fmaxf((chan(c) - mean) * rstd * ln0s[c], 0.0f),
-                                                       fmaxf((chan(c + 1) - mean) * rstd * ln0s[c + 1], 0.0f));
-        *reinterpret_cast<__nv_bfloat162*>(xdst + c) = keep ? o : __floats2bfloat162_rn(0.f, 0.f);
-        if (t == 3) *reinterpret_cast<__nv_bfloat162*>(sp_out + fq * 128 + c) = o;
+      // mel value feeding tap k of position (t, f): rows 2t..2t+2, padded columns 2f..2f+2
+      auto xval = [&](int f, int k) {
+        return k < 9 ? mels[(2 * t + k / 3) * 130 + 2 * f + k % 3] : 0.0f;
+      };
+#pragma unroll 1
+      for (int half = 0; half < 2; ++half) {
+        const int f0 = (warp & 1) * 32 + half * 16;
+        const int fa = f0 + g, fb = fa + 8;
+        const uint32_t a0 = pack_f16x2(xval(fa, 2 * tq), xval(fa, 2 * tq + 1));
+        const uint32_t a1 = pack_f16x2(xval(fb, 2 * tq), xval(fb, 2 * tq + 1));
+        const uint32_t a2 = pack_f16x2(xval(fa, 2 * tq + 8), xval(fa, 2 * tq + 9));
+        const uint32_t a3 = pack_f16x2(xval(fb, 2 * tq + 8), xval(fb, 2 * tq + 9));
+        float acc[16][4];
+#pragma unroll
+        for (int nt = 0; nt < 16; ++nt) {
+          acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+          mma_f16_16816(acc[nt], a0, a1, a2, a3, w0b[nt][0], w0b[nt][1]);
+        }
+        float sa = 0.f, sb = 0.f;
+#pragma unroll
+        for (int nt = 0; nt < 16; ++nt) {
+          sa += acc[nt][0] + acc[nt][1];
+          sb += acc[nt][2] + acc[nt][3];
+        }
+        sa += __shfl_xor_sync(0xffffffffu, sa, 1);
+        sa += __shfl_xor_sync(0xffffffffu, sa, 2);
+        sb += __shfl_xor_sync(0xffffffffu, sb, 1);
+        sb += __shfl_xor_sync(0xffffffffu, sb, 2);
+        const float ma = sa * (1.0f / 128.0f), mb = sb * (1.0f / 128.0f);
+        float va = 0.f, vb = 0.f;
+#pragma unroll
+        for (int nt = 0; nt < 16; ++nt) {
+          va = fmaf(acc[nt][0] - ma, acc[nt][0] - ma, fmaf(acc[nt][1] - ma, acc[nt][1] - ma, va));
+          vb = fmaf(acc[nt][2] - mb, acc[nt][2] - mb, fmaf(acc[nt][3] - mb, acc[nt][3] - mb, vb));
+        }
+        va += __shfl_xor_sync(0xffffffffu, va, 1);
+        va += __shfl_xor_sync(0xffffffffu, va, 2);
+        vb += __shfl_xor_sync(0xffffffffu, vb, 1);
+        vb += __shfl_xor_sync(0xffffffffu, vb, 2);
+        const float ra = rsqrtf(va * (1.0f / 128.0f) + a.eps), rbv = rsqrtf(vb * (1.0f / 128.0f) + a.eps);
+        __nv_bfloat16* xa_row = xin + ((1 + t) * 66 + fa + 1) * kCiPad;
+        __nv_bfloat16* xb_row = xin + ((1 + t) * 66 + fb + 1) * kCiPad;
+#pragma unroll
+        for (int nt = 0; nt < 16; ++nt) {
+          const int ch = nt * 8 + 2 * tq;
+          const float2 lw = *reinterpret_cast<const float2*>(ln0s + ch);
+          const __nv_bfloat162 oa = __floats2bfloat162_rn(fmaxf((acc[nt][0] - ma) * ra * lw.x, 0.0f),
+                                                          fmaxf((acc[nt][1] - ma) * ra * lw.y, 0.0f));
+          const __nv_bfloat162 ob = __floats2bfloat162_rn(fmaxf((acc[nt][2] - mb) * rbv * lw.x, 0.0f),
+                                                          fmaxf((acc[nt][3] - mb) * rbv * lw.y, 0.0f));
+          const __nv_bfloat162 z = __floats2bfloat162_rn(0.f, 0.f);
+          *reinterpret_cast<__nv_bfloat162*>(xa_row + ch) = keep ? oa : z;
+          *reinterpret_cast<__nv_bfloat162*>(xb_row + ch) = keep ? ob : z;
+          if (t == 3) {
+            *reinterpret_cast<__nv_bfloat162*>(sp_out + fa * 128 + ch) = oa;
+            *reinterpret_cast<__nv_bfloat162*>(sp_out + fb * 128 + ch) = ob;
+          }
+        }
       }
     }
     __syncthreads();

@@ -135,11 +135,13 @@ struct RowFusedDev {
 __global__ void __launch_bounds__(256) row_fused_kernel(RowFusedDev a) {
   __shared__ float sh[32];
   const int t = blockIdx.x;
-  if (t >= a.counts[1]) return;
   const int e0 = threadIdx.x * 8;
   const size_t base = static_cast<size_t>(t) * a.d + e0;
-  // every input is requested up front: the row, the GEMM output and the (read
-  // only) norm weights, so the row costs one memory round trip before its stores
+  // every input is requested up front, together with the live token count: the
+  // row (in bounds for every token of the bucket), the GEMM output and the
+  // (read only) norm weights, so the row costs one memory round trip before its
+  // stores
+  const int n_tok = a.counts[1];
   float hv[8], yv[8], pw[8], ow[8], qw[8];
   load8(a.h + base, hv);
   if (a.y) load8(a.y + base, yv);
@@ -148,6 +150,7 @@ __global__ void __launch_bounds__(256) row_fused_kernel(RowFusedDev a) {
   if (a.post_w) load8_nc(a.post_w + e0, pw);
   if (a.out_w) load8_nc(a.out_w + e0, ow);
   if (a.xa && a.pre_norm && a.pre_w) load8_nc(a.pre_w + e0, qw);
+  if (t >= n_tok) return;
   if (a.y) {
     if (a.post_w) {
 #pragma unroll
@@ -185,7 +188,7 @@ struct LconvDev {
   const float* dw;           // [5][d] tap-major
   const float* norm_w;       // [d]
   __nv_bfloat16* xa;         // [tok][d]
-  int layer, layers, d, slots;
+  int layer, layers, d, slots, rows_cap;
   float eps, clip, in_lo, in_hi;
   bool f16;  // xa holds fp16 (int8-weight GEMM input) instead of bf16
 };
@@ -197,10 +200,12 @@ template <int G>
 __global__ void __launch_bounds__(128) lconv_kernel(LconvDev a) {
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (row >= a.counts[0]) return;
+  const int n_rows = a.counts[0];
+  const int rl = min(row, a.rows_cap - 1);  // the grid rounds the bucket up to whole CTAs
+  const int slot = a.row_slot[rl];
+  const SlotMeta m = a.row_meta[rl];
+  if (row >= n_rows) return;
   const int d = G * 256;
-  const int slot = a.row_slot[row];
-  const SlotMeta m = a.row_meta[row];
   const size_t rb = ring_base(slot, a.layer, a.slots, kConvRing, d);
   const int first_real = 4 - min(m.fill, 4);  // ring rows written since the last reset
   float cv[2][G][8];
@@ -411,6 +416,7 @@ cudaError_t launch_lconv(Ctx& c, int layer, int rows_cap, cudaStream_t s) {
   a.layers = c.cfg.layers;
   a.d = c.cfg.hidden;
   a.slots = c.cfg.max_sessions;
+  a.rows_cap = rows_cap;
   a.eps = c.cfg.rms_eps;
   a.clip = c.cfg.gradient_clipping;
   a.in_lo = c.w.layers[layer].clip[7][0];  // linear_end input bounds
