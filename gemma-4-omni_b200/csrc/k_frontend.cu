@@ -5,8 +5,9 @@
 // (duplex_kernel/listener.py:1807-1850): [160-sample tail | 1280 PCM | 0] ->
 // eight 320-sample frames at hop 160, times the periodic Hann window (the
 // product is formed in fp32 exactly as the reference's float32 NumPy does),
-// 512-point real DFT magnitude, HTK mel filterbank, log(x + 1e-3).  One CTA
-// per session; the DFT uses exact twiddles from a 512-entry table.
+// 512-point real DFT magnitude (a 256-point complex FFT and the real-input
+// split, exact twiddles from a 512-entry table), HTK mel filterbank,
+// log(x + 1e-3).  One CTA per session.
 //
 // subsample_kernel restates the streaming subsampler
 // (duplex_kernel/streaming_conformer.py:741-761, _stream_subsample_layer
@@ -14,9 +15,9 @@
 // models/gemma4/modeling_gemma4.py:317-372): conv0 (1 -> 128 channels) +
 // LayerNorm(128) + ReLU over [cached mel row | 8 new rows], then conv1
 // (128 -> C1) + LayerNorm(C1) + ReLU over [cached conv0 row | 4 new rows].
-// conv0 runs on CUDA cores (9 taps); conv1 is an implicit GEMM
-// [64 positions x 1152] x [1152 x C1] on mma.sync bf16 tensor-core tiles with
-// fp32 accumulation.  The output is the bf16 input of the input projection.
+// conv0 is [256 positions x 16 (9) taps] x [16 x 128] on mma.sync fp16 tiles;
+// conv1 is an implicit GEMM [64 positions x 1152] x [1152 x C1] on mma.sync
+// bf16 tiles; both accumulate in fp32.  The output is the bf16 input of the input projection.
 #include "common.cuh"
 #include "listener.h"
 
@@ -38,9 +39,15 @@ struct MelArgs {
   const int2* filter_range;                          // [128] (k_lo, k_hi)
 };
 
+// |X[k]|, k = 0..256, of the 512-point real DFT of each frame (zero-padded from
+// 320 samples), computed as a 256-point complex FFT of z[m] = x[2m] + i x[2m+1]
+// followed by the real-input split X[k] = E[k] + W^k O[k] with
+// E = (Z[k] + conj Z[256-k]) / 2, O = (Z[k] - conj Z[256-k]) / 2i and
+// W = exp(-2 pi i / 512).  Radix-2 decimation in time, bit-reversed input,
+// exact twiddles cos/sin(2 pi j / 512) from the table; fp32 throughout.
 __global__ void __launch_bounds__(256) mel_kernel(MelArgs a) {
   const int row = blockIdx.x;
-  __shared__ float x[kFrames * kWin];
+  __shared__ float zr[kFrames][256], zi[kFrames][256];
   __shared__ float mag[kFrames][kBins + 3];
   __shared__ float ct[512], st[512];
   // row tables (in bounds for every row of the bucket) read with the live count
@@ -57,40 +64,53 @@ __global__ void __launch_bounds__(256) mel_kernel(MelArgs a) {
     ct[i] = a.cos_tab[i];
     st[i] = a.sin_tab[i];
   }
-  // frame f covers padded samples [160 f, 160 f + 320) of [tail | pcm | 0]
-  for (int i = threadIdx.x; i < kFrames * kWin; i += blockDim.x) {
-    const int f = i / kWin, n = i % kWin;
-    const int sidx = f * 160 + n;  // index into padded (1441 samples)
-    float v;
-    if (sidx < kTail) {
-      v = fresh ? 0.0f : tail_in[sidx];
-    } else {
-      v = pcm[sidx - kTail];  // sidx <= 7*160+319 = 1439 < 1440: never the pad sample
-    }
-    x[i] = v * a.window[n];
+  // frame f covers padded samples [160 f, 160 f + 320) of [tail | pcm | 0]; the
+  // windowed product is formed in fp32 as the reference's float32 NumPy does
+  auto sample = [&](int f, int n) {
+    if (n >= kWin) return 0.0f;
+    const int sidx = f * 160 + n;  // index into the padded signal (never the final pad sample)
+    const float v = sidx < kTail ? (fresh ? 0.0f : tail_in[sidx]) : pcm[sidx - kTail];
+    return v * a.window[n];
+  };
+  for (int i = threadIdx.x; i < kFrames * 256; i += blockDim.x) {
+    const int f = i >> 8, m = i & 255;
+    const int r = static_cast<int>(__brev(static_cast<unsigned>(m)) >> 24);
+    zr[f][r] = sample(f, 2 * m);
+    zi[f][r] = sample(f, 2 * m + 1);
   }
   __syncthreads();
   // staged tail for the next tick: last 160 PCM samples
   float* tail_out = a.tail + (static_cast<size_t>(slot) * 2 + (parity ^ 1)) * kTail;
   for (int i = threadIdx.x; i < kTail; i += blockDim.x) tail_out[i] = pcm[kPcm - kTail + i];
-  // DFT magnitudes: thread k -> bin k for all frames (bin 256 by thread 0)
-  for (int k = threadIdx.x; k < kBins; k += blockDim.x) {
-    float re[kFrames], im[kFrames];
-#pragma unroll
-    for (int f = 0; f < kFrames; ++f) re[f] = im[f] = 0.0f;
-    int idx = 0;
-    for (int n = 0; n < kWin; ++n) {
-      const float c = ct[idx], s = st[idx];
-#pragma unroll
-      for (int f = 0; f < kFrames; ++f) {
-        const float xv = x[f * kWin + n];
-        re[f] = fmaf(xv, c, re[f]);
-        im[f] = fmaf(xv, s, im[f]);
-      }
-      idx = (idx + k) & 511;
+  // 256-point complex FFT of every frame, 8 stages
+  for (int len = 2, tstep = 256; len <= 256; len <<= 1, tstep >>= 1) {
+    const int half = len >> 1;
+    for (int b = threadIdx.x; b < kFrames * 128; b += blockDim.x) {
+      const int f = b >> 7, j = b & 127;
+      const int pos = j & (half - 1);
+      const int i0 = (j - pos) * 2 + pos, i1 = i0 + half;
+      const float wr = ct[pos * tstep], wi = -st[pos * tstep];  // exp(-2 pi i pos / len)
+      const float br = zr[f][i1], bi = zi[f][i1];
+      const float tr = br * wr - bi * wi, ti = br * wi + bi * wr;
+      const float ar = zr[f][i0], ai = zi[f][i0];
+      zr[f][i0] = ar + tr;
+      zi[f][i0] = ai + ti;
+      zr[f][i1] = ar - tr;
+      zi[f][i1] = ai - ti;
     }
-#pragma unroll
-    for (int f = 0; f < kFrames; ++f) mag[f][k] = sqrtf(re[f] * re[f] + im[f] * im[f]);
+    __syncthreads();
+  }
+  // real-input split -> magnitudes of bins 0..256
+  for (int o = threadIdx.x; o < kFrames * kBins; o += blockDim.x) {
+    const int f = o / kBins, k = o % kBins;
+    const int k1 = k & 255, k2 = (256 - k) & 255;
+    const float zkr = zr[f][k1], zki = zi[f][k1];
+    const float ckr = zr[f][k2], cki = -zi[f][k2];  // conj Z[256 - k]
+    const float er = 0.5f * (zkr + ckr), ei = 0.5f * (zki + cki);
+    const float orr = 0.5f * (zki - cki), oi = -0.5f * (zkr - ckr);  // (Z - conj Z') / 2i
+    const float wr = ct[k], wi = -st[k];                              // exp(-2 pi i k / 512)
+    const float xr = er + (orr * wr - oi * wi), xi = ei + (orr * wi + oi * wr);
+    mag[f][k] = sqrtf(xr * xr + xi * xi);
   }
   __syncthreads();
   // mel filterbank (sparse row ranges) + log

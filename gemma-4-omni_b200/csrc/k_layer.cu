@@ -83,6 +83,44 @@ __device__ __forceinline__ void store8_bf16(__nv_bfloat16* p, const float (&v)[8
   *reinterpret_cast<int4*>(p) = r;
 }
 
+// Two block sums at once (one set of barriers); sh holds >= 64 floats.
+__device__ __forceinline__ float2 block_sum2(float2 v, float* sh) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  v.x = warp_sum(v.x);
+  v.y = warp_sum(v.y);
+  __syncthreads();
+  if (lane == 0) {
+    sh[warp] = v.x;
+    sh[32 + warp] = v.y;
+  }
+  __syncthreads();
+  float2 t = make_float2(0.f, 0.f);
+  for (int i = 0; i < nw; ++i) {
+    t.x += sh[i];
+    t.y += sh[32 + i];
+  }
+  return t;
+}
+
+// RMSNorm of the same 8-element slice of two rows, weights in registers.
+__device__ __forceinline__ void rms8w2(float (&v0)[8], float (&v1)[8], const float (&w8)[8], int d, float eps,
+                                       float* sh) {
+  float2 ss = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    ss.x = fmaf(v0[i], v0[i], ss.x);
+    ss.y = fmaf(v1[i], v1[i], ss.y);
+  }
+  ss = block_sum2(ss, sh);
+  const float r0 = rsqrtf(ss.x / static_cast<float>(d) + eps);
+  const float r1 = rsqrtf(ss.y / static_cast<float>(d) + eps);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    v0[i] = v0[i] * r0 * w8[i];
+    v1[i] = v1[i] * r1 * w8[i];
+  }
+}
+
 // RMSNorm with the weights already in registers (w8: this thread's 8 weights).
 __device__ __forceinline__ void rms8w(float (&v)[8], const float (&w8)[8], int d, float eps, float* sh) {
   float ss = 0.f;
@@ -131,50 +169,76 @@ struct RowFusedDev {
   bool f16;  // xa holds fp16 (int8-weight GEMM input) instead of bf16
 };
 
-// One CTA of d/8 threads per token row, 8 contiguous elements per thread.
+// One CTA of d/8 threads per session row, i.e. both tick tokens (the live token
+// count is always even), 8 contiguous elements of each token per thread; the
+// two tokens' norms share their block reductions.  Half as many CTAs as
+// tokens keeps a 2048-token step within one wave of resident CTAs.
 __global__ void __launch_bounds__(256) row_fused_kernel(RowFusedDev a) {
-  __shared__ float sh[32];
-  const int t = blockIdx.x;
+  __shared__ float sh[64];
+  const int t0 = 2 * blockIdx.x;
   const int e0 = threadIdx.x * 8;
-  const size_t base = static_cast<size_t>(t) * a.d + e0;
+  const size_t base0 = static_cast<size_t>(t0) * a.d + e0, base1 = base0 + a.d;
   // every input is requested up front, together with the live token count: the
-  // row (in bounds for every token of the bucket), the GEMM output and the
-  // (read only) norm weights, so the row costs one memory round trip before its
-  // stores
+  // rows (in bounds for every token of the bucket), the GEMM outputs and the
+  // (read only) norm weights -- one memory round trip before the stores
   const int n_tok = a.counts[1];
-  float hv[8], yv[8], pw[8], ow[8], qw[8];
-  load8(a.h + base, hv);
-  if (a.y) load8(a.y + base, yv);
+  float h0[8], h1[8], y0[8], y1[8], pw[8], ow[8], qw[8];
+  load8(a.h + base0, h0);
+  load8(a.h + base1, h1);
+  if (a.y) {
+    load8(a.y + base0, y0);
+    load8(a.y + base1, y1);
+  }
 #pragma unroll
   for (int i = 0; i < 8; ++i) pw[i] = ow[i] = qw[i] = 1.0f;
   if (a.post_w) load8_nc(a.post_w + e0, pw);
   if (a.out_w) load8_nc(a.out_w + e0, ow);
   if (a.xa && a.pre_norm && a.pre_w) load8_nc(a.pre_w + e0, qw);
-  if (t >= n_tok) return;
+  if (t0 >= n_tok) return;
   if (a.y) {
     if (a.post_w) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) yv[i] = fminf(fmaxf(yv[i], -a.clip), a.clip);
-      rms8w(yv, pw, a.d, a.eps, sh);
+      for (int i = 0; i < 8; ++i) {
+        y0[i] = fminf(fmaxf(y0[i], -a.clip), a.clip);
+        y1[i] = fminf(fmaxf(y1[i], -a.clip), a.clip);
+      }
+      rms8w2(y0, y1, pw, a.d, a.eps, sh);
     }
 #pragma unroll
-    for (int i = 0; i < 8; ++i) hv[i] = a.residual ? fmaf(yv[i], a.alpha, hv[i]) : yv[i] * a.alpha;
+    for (int i = 0; i < 8; ++i) {
+      h0[i] = a.residual ? fmaf(y0[i], a.alpha, h0[i]) : y0[i] * a.alpha;
+      h1[i] = a.residual ? fmaf(y1[i], a.alpha, h1[i]) : y1[i] * a.alpha;
+    }
   }
   if (a.out_w) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) hv[i] = fminf(fmaxf(hv[i], -a.clip), a.clip);
-    rms8w(hv, ow, a.d, a.eps, sh);
+    for (int i = 0; i < 8; ++i) {
+      h0[i] = fminf(fmaxf(h0[i], -a.clip), a.clip);
+      h1[i] = fminf(fmaxf(h1[i], -a.clip), a.clip);
+    }
+    rms8w2(h0, h1, ow, a.d, a.eps, sh);
   }
-  store8(a.h + base, hv);
-  if (a.dbg) store8(a.dbg + base, hv);
+  store8(a.h + base0, h0);
+  store8(a.h + base1, h1);
+  if (a.dbg) {
+    store8(a.dbg + base0, h0);
+    store8(a.dbg + base1, h1);
+  }
   if (a.xa) {
-    float xv[8];
+    float x0[8], x1[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) xv[i] = a.pre_clamp ? fminf(fmaxf(hv[i], -a.clip), a.clip) : hv[i];
-    if (a.pre_norm) rms8w(xv, qw, a.d, a.eps, sh);
+    for (int i = 0; i < 8; ++i) {
+      x0[i] = a.pre_clamp ? fminf(fmaxf(h0[i], -a.clip), a.clip) : h0[i];
+      x1[i] = a.pre_clamp ? fminf(fmaxf(h1[i], -a.clip), a.clip) : h1[i];
+    }
+    if (a.pre_norm) rms8w2(x0, x1, qw, a.d, a.eps, sh);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) xv[i] = fminf(fmaxf(xv[i], a.in_lo), a.in_hi);
-    store8_act(a.xa + base, xv, a.f16);
+    for (int i = 0; i < 8; ++i) {
+      x0[i] = fminf(fmaxf(x0[i], a.in_lo), a.in_hi);
+      x1[i] = fminf(fmaxf(x1[i], a.in_lo), a.in_hi);
+    }
+    store8_act(a.xa + base0, x0, a.f16);
+    store8_act(a.xa + base1, x1, a.f16);
   }
 }
 
@@ -398,7 +462,7 @@ cudaError_t launch_row_fused(Ctx& c, int tok_cap, const RowFusedArgs& r, cudaStr
   a.xa = r.xa;
   a.dbg = r.dbg;
   a.f16 = c.weight_int8 != 0;
-  row_fused_kernel<<<tok_cap, c.cfg.hidden / 8, 0, s>>>(a);
+  row_fused_kernel<<<tok_cap / 2, c.cfg.hidden / 8, 0, s>>>(a);  // one CTA per session (2 tokens)
   return cudaGetLastError();
 }
 
