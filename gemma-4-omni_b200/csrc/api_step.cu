@@ -1091,8 +1091,19 @@ int lb_step_host(lb_ctx* x, int n, const int32_t* handles, const int64_t* keys, 
   cudaSetDevice(c.device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   char* p = static_cast<char*>(x->pinned);
+  // page-locked caller buffers are copied by DMA directly; pageable ones go
+  // through the context's pinned staging area
+  auto pinned = [](const void* ptr) {
+    cudaPointerAttributes at{};
+    if (cudaPointerGetAttributes(&at, ptr) != cudaSuccess) {
+      cudaGetLastError();
+      return false;
+    }
+    return at.type == cudaMemoryTypeHost;
+  };
   auto stage = [&](const void* src, size_t bytes) -> void* {
     if (!src) return nullptr;
+    if (pinned(src)) return const_cast<void*>(src);
     char* dst = p;
     std::memcpy(dst, src, bytes);
     p += align_up(bytes, 256);
@@ -1115,6 +1126,12 @@ int lb_step_host(lb_ctx* x, int n, const int32_t* handles, const int64_t* keys, 
   char* o_film = o_soft + align_up(soft_b, 256);
   if (static_cast<size_t>(o_film + film_b - static_cast<char*>(x->pinned)) > x->pinned_bytes)
     return LB_ERR_CAPACITY;
+  const bool raw_direct = out_raw && pinned(out_raw);
+  const bool soft_direct = out_soft && pinned(out_soft);
+  const bool film_direct = out_film && pinned(out_film);
+  if (raw_direct) o_raw = static_cast<char*>(out_raw);
+  if (soft_direct) o_soft = static_cast<char*>(out_soft);
+  if (film_direct) o_film = static_cast<char*>(out_film);
   int rc = lb_pack_async(x, n, static_cast<int32_t*>(ph), static_cast<int64_t*>(pk),
                          static_cast<int64_t*>(pf), static_cast<int64_t*>(pq),
                          static_cast<uint8_t*>(pm), stream);
@@ -1127,9 +1144,9 @@ int lb_step_host(lb_ctx* x, int n, const int32_t* handles, const int64_t* keys, 
     if (rc) return rc;
   }
   if (cudaStreamSynchronize(s) != cudaSuccess) return LB_ERR_CUDA;
-  if (out_raw) std::memcpy(out_raw, o_raw, raw_b);
-  if (out_soft) std::memcpy(out_soft, o_soft, soft_b);
-  if (out_film) std::memcpy(out_film, o_film, film_b);
+  if (out_raw && !raw_direct) std::memcpy(out_raw, o_raw, raw_b);
+  if (out_soft && !soft_direct) std::memcpy(out_soft, o_soft, soft_b);
+  if (out_film && !film_direct) std::memcpy(out_film, o_film, film_b);
   return LB_OK;
 }
 

@@ -201,10 +201,21 @@ def test_ragged_continuous_batching_matches_oracle(pkg):
     eng.close()
 
 
-def test_step_host_matches_device_path(pkg):
-    """lb_step_host (host buffers, H2D/D2H inside the call) equals lb_step_async outputs."""
+@pytest.mark.parametrize("pinned", [False, True])
+def test_step_host_matches_device_path(pkg, pinned):
+    """lb_step_host (host buffers, H2D/D2H inside the call) equals lb_step_async
+    outputs, with pageable buffers (staged) and page-locked ones (direct DMA)."""
     from gemma4_omni_b200 import _lib, synthetic
     from gemma4_omni_b200.config import SMALL
+
+    def host(a):
+        if not pinned:
+            return a
+        t = torch.empty(a.shape, dtype={np.uint16: torch.int16, np.float32: torch.float32}[a.dtype.type],
+                        pin_memory=True)
+        out = t.numpy().view(a.dtype)  # the array's base keeps the pinned tensor alive
+        out[...] = a
+        return out
 
     n = 5
     a = make_engine(SMALL, 1, sessions=8)
@@ -219,10 +230,10 @@ def test_step_host_matches_device_path(pkg):
                torch.from_numpy(frames).cuda())
         oa = a.step(torch.from_numpy(pcm).cuda(), kind=_lib.LB_INPUT_PCM, query=query.cuda())
         a.commit()
-        soft = np.zeros((n, 2, SMALL.text_hidden), np.uint16)
-        film = np.zeros((n, 2, SMALL.film_query_dim), np.uint16)
-        qb = query.view(torch.int16).numpy().view(np.uint16)
-        b.step_host(handles, keys, frames, frames.copy(), pcm, query=qb, out_soft=soft, out_film=film)
+        soft = host(np.zeros((n, 2, SMALL.text_hidden), np.uint16))
+        film = host(np.zeros((n, 2, SMALL.film_query_dim), np.uint16))
+        qb = host(query.view(torch.int16).numpy().view(np.uint16))
+        b.step_host(handles, keys, frames, frames.copy(), host(pcm), query=qb, out_soft=soft, out_film=film)
         # same kernels; only the fp32 split-K reduction order may differ between runs
         as_f32 = lambda u: torch.from_numpy((u.astype(np.uint32) << 16).view(np.float32))
         assert_parity(oa["soft"], as_f32(soft), "step_host soft", 0.99999, 1e-2)
