@@ -215,14 +215,22 @@ __host__ __device__ constexpr uint32_t umma_idesc_f16(int m, int n) {
 // (int8 widens to fp16 in two integer ops; fp16 keeps 3 more mantissa bits).
 // fp16 stores saturate at +/-65504 instead of overflowing to infinity.
 constexpr float kF16Max = 65504.0f;
+// fp16 with saturation in one instruction: |v| beyond the largest finite fp16
+// becomes +/-65504 (the same result as clamping to +/-65504 and rounding)
+__device__ __forceinline__ uint16_t f16_bits_satfinite(float v) {
+  uint16_t h;
+  asm("cvt.rn.satfinite.f16.f32 %0, %1;" : "=h"(h) : "f"(v));
+  return h;
+}
 __device__ __forceinline__ uint16_t act_bits(float v, bool f16) {
-  if (f16) return __half_as_ushort(__float2half_rn(fminf(fmaxf(v, -kF16Max), kF16Max)));
+  if (f16) return f16_bits_satfinite(v);
   return __bfloat16_as_ushort(__float2bfloat16_rn(v));
 }
 __device__ __forceinline__ uint32_t act_bits2(float a, float b, bool f16) {
   if (f16) {
-    const __half2 h = __floats2half2_rn(fminf(fmaxf(a, -kF16Max), kF16Max), fminf(fmaxf(b, -kF16Max), kF16Max));
-    return *reinterpret_cast<const uint32_t*>(&h);
+    uint32_t h;  // a -> low half, b -> high half (cvt puts its first source in the high half)
+    asm("cvt.rn.satfinite.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(b), "f"(a));
+    return h;
   }
   const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<const uint32_t*>(&h);

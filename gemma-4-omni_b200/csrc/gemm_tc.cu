@@ -169,14 +169,17 @@ __device__ __forceinline__ Unit unit_of(int u, int o_tiles, int t_tiles, int TN,
 // int8 scale, bias, output clamp, optional SiLU of the bf16-rounded linear
 // output, next-input clamp.  Branch-free over the columns so the NC
 // independent chains interleave.
-template <bool SILU, int NC>
+// CLAMP = false when all four bounds are infinite (the clamps are the identity
+// then), which halves the instructions per value of a fp32 or bf16 store.
+template <bool SILU, bool CLAMP, int NC>
 __device__ __forceinline__ void epilogue_math(const uint32_t (&r)[NC], float (&y)[NC], float scale,
                                               float bias, float lo, float hi, float plo, float phi) {
 #pragma unroll
   for (int j = 0; j < NC; ++j) {
-    float v = fminf(fmaxf(fmaf(__uint_as_float(r[j]), scale, bias), lo), hi);
+    float v = fmaf(__uint_as_float(r[j]), scale, bias);
+    if (CLAMP) v = fminf(fmaxf(v, lo), hi);
     if (SILU) v = silu_tanh(bf16_round(v));
-    y[j] = fminf(fmaxf(v, plo), phi);
+    y[j] = CLAMP ? fminf(fmaxf(v, plo), phi) : v;
   }
 }
 
@@ -324,6 +327,7 @@ __global__ void __launch_bounds__(GemmCfg<TN, WK>::kThreads, 1)
     // clamps of the linear output (bf16 / fp32 stores) and of the next input
     const float lo = p.out_mode == 2 ? -INFINITY : p.out_lo, hi = p.out_mode == 2 ? INFINITY : p.out_hi;
     const float plo = p.out_mode == 0 ? p.post_lo : -INFINITY, phi = p.out_mode == 0 ? p.post_hi : INFINITY;
+    const bool clamps = isfinite(lo) || isfinite(hi) || isfinite(plo) || isfinite(phi);
     int local = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
       const Unit w = unit_of(u, o_tiles, t_tiles, TN, p.kb_per_split, total_kb);
@@ -342,10 +346,16 @@ __global__ void __launch_bounds__(GemmCfg<TN, WK>::kThreads, 1)
       constexpr int NC = Cfg::kCols;
       auto drain = [&](const uint32_t (&r)[NC], int c) {
         float y[NC];
-        if (silu) {
-          epilogue_math<true, NC>(r, y, scale, bias, lo, hi, plo, phi);
+        if (clamps) {
+          if (silu) {
+            epilogue_math<true, true, NC>(r, y, scale, bias, lo, hi, plo, phi);
+          } else {
+            epilogue_math<false, true, NC>(r, y, scale, bias, lo, hi, plo, phi);
+          }
+        } else if (silu) {
+          epilogue_math<true, false, NC>(r, y, scale, bias, lo, hi, plo, phi);
         } else {
-          epilogue_math<false, NC>(r, y, scale, bias, lo, hi, plo, phi);
+          epilogue_math<false, false, NC>(r, y, scale, bias, lo, hi, plo, phi);
         }
         const size_t base = static_cast<size_t>(w.t0 + c) * ld + o;
         const int n = c_end - c;  // >= 1
