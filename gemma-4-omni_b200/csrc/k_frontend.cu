@@ -204,43 +204,77 @@ __global__ void __launch_bounds__(kSubThreads, 1) subsample_kernel(SubArgs a) {
       w0b[nt][1] = pack_f16x2(tap(2 * tq + 8), tap(2 * tq + 9));
     }
   }
+  // the frequency padding columns of the mel tile are zero for every row
+  for (int i = tid; i < 9 * 2; i += blockDim.x) mels[(i >> 1) * 130 + ((i & 1) ? 129 : 0)] = 0.0f;
   const int n_rows = a.counts[0];
-  for (int row = blockIdx.x; row < n_rows; row += gridDim.x) {
+  // row tables of this CTA's first row; each iteration fetches the next row's
+  // with its own data loads, so a row costs one memory round trip
+  int row = blockIdx.x;
+  int slot = 0, mask = 0;
+  SlotMeta m{};
+  if (row < n_rows) {
+    slot = a.row_slot[row];
+    m = a.row_meta[row];
+    mask = a.row_mask[row];
+  }
+  for (; row < n_rows; row += gridDim.x) {
     __syncthreads();
-    const int slot = a.row_slot[row];
-    const SlotMeta m = a.row_meta[row];
     const int parity = (m.pos >> 1) & 1;
-    const int mask = a.row_mask[row];
-    const float mel_prev_ok = (m.flags & 1) ? 1.0f : 0.0f;
-    const float sub_prev_ok = (m.flags & 2) ? 1.0f : 0.0f;
+    const bool mel_prev_ok = (m.flags & 1) != 0;
+    const bool sub_prev_ok = (m.flags & 2) != 0;
     const float* mel_in = a.mel + static_cast<size_t>(row) * 8 * kMelBins;
-    float* mp_in = a.mel_prev + (static_cast<size_t>(slot) * 2 + parity) * kMelBins;
+    const float* mp_in = a.mel_prev + (static_cast<size_t>(slot) * 2 + parity) * kMelBins;
     float* mp_out = a.mel_prev + (static_cast<size_t>(slot) * 2 + (parity ^ 1)) * kMelBins;
-    // masked mel rows (row 0 = cached row), frequency-padded by one zero each side
-    for (int i = tid; i < 9 * 130; i += blockDim.x) {
-      const int r = i / 130, fq = i % 130 - 1;
-      float v = 0.0f;
-      if (fq >= 0 && fq < kMelBins) {
-        if (r == 0) {
-          v = mp_in[fq] * mel_prev_ok;
-        } else {
-          v = ((mask >> (r - 1)) & 1) ? mel_in[(r - 1) * kMelBins + fq] : 0.0f;
-        }
-      }
-      mels[i] = v;
+    const __nv_bfloat16* sp_in = a.sub_prev + (static_cast<size_t>(slot) * 2 + parity) * kF0 * 128;
+    // ---- every global load of this row in flight together: the 8 new mel rows
+    // (4 floats per thread), the cached mel row (threads 0..31), the cached
+    // conv0 row (16 KB: four 16-byte chunks per thread) and the next row's tables
+    float4 mv = __ldg(reinterpret_cast<const float4*>(mel_in) + tid);  // 256 x 4 = 8 x 128
+    float4 pv = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (tid < 32 && mel_prev_ok) pv = __ldg(reinterpret_cast<const float4*>(mp_in) + tid);
+    int4 sv[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      sv[q] = sub_prev_ok ? __ldg(reinterpret_cast<const int4*>(sp_in) + tid + q * kSubThreads)
+                          : make_int4(0, 0, 0, 0);
     }
-    // cached conv0 row -> conv1 input row 0
-    const __nv_bfloat16* sp_in =
-        a.sub_prev + (static_cast<size_t>(slot) * 2 + parity) * kF0 * 128;
-    for (int i = tid; i < kF0 * 64; i += blockDim.x) {  // 64 freq x 64 channel pairs
-      const int fq = i / 64, cp = i % 64;
-      __nv_bfloat162 v = reinterpret_cast<const __nv_bfloat162*>(sp_in)[fq * 64 + cp];
-      if (sub_prev_ok == 0.0f) v = __floats2bfloat162_rn(0.0f, 0.0f);
-      reinterpret_cast<__nv_bfloat162*>(xin + (0 * 66 + fq + 1) * kCiPad)[cp] = v;
+    const int next = row + gridDim.x;
+    int n_slot = slot, n_mask = mask;
+    SlotMeta n_m = m;
+    if (next < n_rows) {
+      n_slot = a.row_slot[next];
+      n_m = a.row_meta[next];
+      n_mask = a.row_mask[next];
+    }
+    // masked mel rows (row 0 = cached row), frequency-padded by one zero each side
+    {
+      const int r = tid >> 5, f4 = (tid & 31) * 4;  // new mel row r (0..7), frequencies f4..f4+3
+      const bool keep = (mask >> r) & 1;
+      float* dst = mels + (r + 1) * 130 + 1 + f4;
+      dst[0] = keep ? mv.x : 0.f;
+      dst[1] = keep ? mv.y : 0.f;
+      dst[2] = keep ? mv.z : 0.f;
+      dst[3] = keep ? mv.w : 0.f;
+      if (tid < 32) {
+        float* d0 = mels + 1 + tid * 4;
+        d0[0] = pv.x;
+        d0[1] = pv.y;
+        d0[2] = pv.z;
+        d0[3] = pv.w;
+      }
+      // staged mel_prev = last mel row (unmasked)
+      if (r == 7) *reinterpret_cast<float4*>(mp_out + f4) = mv;
+    }
+    // cached conv0 row -> conv1 input row 0 (16-byte chunk c = 8 channels of one frequency)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int c = tid + q * kSubThreads;
+      const int fq = c >> 4, c8 = (c & 15) * 8;
+      uint2* dst = reinterpret_cast<uint2*>(xin + (0 * 66 + fq + 1) * kCiPad + c8);
+      dst[0] = make_uint2(static_cast<uint32_t>(sv[q].x), static_cast<uint32_t>(sv[q].y));
+      dst[1] = make_uint2(static_cast<uint32_t>(sv[q].z), static_cast<uint32_t>(sv[q].w));
     }
     __syncthreads();
-    // staged mel_prev = last mel row (unmasked)
-    for (int i = tid; i < kMelBins; i += blockDim.x) mp_out[i] = mel_in[7 * kMelBins + i];
     // ---- conv0 + LN(128) + ReLU on the tensor cores: D[pos][ch] = sum_tap A[pos][tap] W0[ch][tap]
     // as one m16n8k16 per (16 positions, 8 channels) -- the 9 taps padded to 16,
     // fp16 operands (the mel rounded to fp16; the bf16-valued weights exactly),
@@ -373,6 +407,9 @@ __global__ void __launch_bounds__(kSubThreads, 1) subsample_kernel(SubArgs a) {
         *reinterpret_cast<uint32_t*>(o + c) = act_bits2(y0, y1, a.f16);
       }
     }
+    slot = n_slot;
+    m = n_m;
+    mask = n_mask;
   }
 }
 

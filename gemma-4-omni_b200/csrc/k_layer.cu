@@ -257,67 +257,91 @@ struct LconvDev {
   bool f16;  // xa holds fp16 (int8-weight GEMM input) instead of bf16
 };
 
-// One warp per session (both tick tokens); lane owns G groups of 8 channels,
-// e = (g*32 + lane)*8, so every load is a whole-warp coalesced 512-byte run and
-// the two RMS reductions are warp shuffles.
-template <int G>
-__global__ void __launch_bounds__(128) lconv_kernel(LconvDev a) {
-  const int lane = threadIdx.x & 31;
-  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+// W warps per session (both tick tokens); warp w of a session owns channel
+// groups [w*G/W, (w+1)*G/W), lane its 8 channels e = (g*32 + lane)*8 of each,
+// so every load is a whole-warp coalesced 512-byte run.  The two RMS
+// reductions are warp shuffles, then (W > 1) a sum over the session's warps in
+// shared memory.  Splitting a session over two warps halves each warp's
+// dependent load chain and doubles the warps per SM, with 1024 sessions still
+// in one wave of 256-thread CTAs.
+template <int G, int W>
+__global__ void __launch_bounds__(256) lconv_kernel(LconvDev a) {
+  constexpr int GW = G / W;  // channel groups per warp
+  static_assert(G % W == 0, "channel groups must split evenly over the session's warps");
+  __shared__ float2 part[8];  // per warp: (sum sq token 0, sum sq token 1)
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int sess = warp / W, w = warp % W;
+  const int row = blockIdx.x * ((blockDim.x >> 5) / W) + sess;
   const int n_rows = a.counts[0];
   const int rl = min(row, a.rows_cap - 1);  // the grid rounds the bucket up to whole CTAs
   const int slot = a.row_slot[rl];
   const SlotMeta m = a.row_meta[rl];
-  if (row >= n_rows) return;
+  const bool live = row < n_rows;
   const int d = G * 256;
   const size_t rb = ring_base(slot, a.layer, a.slots, kConvRing, d);
   const int first_real = 4 - min(m.fill, 4);  // ring rows written since the last reset
-  float cv[2][G][8];
+  float cv[2][GW][8];
   float ss0 = 0.f, ss1 = 0.f;
+  if (live) {
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    const int e0 = (g * 32 + lane) * 8;
-    float win[6][8];
+    for (int gg = 0; gg < GW; ++gg) {
+      const int e0 = ((w * GW + gg) * 32 + lane) * 8;
+      float win[6][8];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      if (j >= first_real) {  // canonical rows: read-only here (the step writes only staged rows)
-        load8_bf16_nc(a.ring + rb + static_cast<size_t>((m.pos + j) & (kConvRing - 1)) * d + e0, win[j]);
-      } else {
+      for (int j = 0; j < 4; ++j) {
+        if (j >= first_real) {  // canonical rows: read-only here (the step writes only staged rows)
+          load8_bf16_nc(a.ring + rb + static_cast<size_t>((m.pos + j) & (kConvRing - 1)) * d + e0, win[j]);
+        } else {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) win[j][i] = 0.f;
+          for (int i = 0; i < 8; ++i) win[j][i] = 0.f;
+        }
       }
-    }
 #pragma unroll
-    for (int t = 0; t < 2; ++t) {
-      float av[8], bv[8];
-      const __nv_bfloat16* gp = a.gl + (static_cast<size_t>(row) * 2 + t) * 2 * d;
-      load8_bf16_nc(gp + e0, av);
-      load8_bf16_nc(gp + d + e0, bv);
+      for (int t = 0; t < 2; ++t) {
+        float av[8], bv[8];
+        const __nv_bfloat16* gp = a.gl + (static_cast<size_t>(row) * 2 + t) * 2 * d;
+        load8_bf16_nc(gp + e0, av);
+        load8_bf16_nc(gp + d + e0, bv);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) win[4 + t][i] = bf16_round(__fdividef(av[i], 1.0f + __expf(-bv[i])));  // GLU
-      store8_bf16(a.ring + rb + static_cast<size_t>((m.pos + 4 + t) & (kConvRing - 1)) * d + e0, win[4 + t]);
-    }
-    float w5t[5][8];  // tap-major weights: 2 vector loads per tap
-#pragma unroll
-    for (int k = 0; k < 5; ++k) load8_nc(a.dw + static_cast<size_t>(k) * d + e0, w5t[k]);
-#pragma unroll
-    for (int t = 0; t < 2; ++t)
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        float acc = 0.f;
-#pragma unroll
-        for (int k = 0; k < 5; ++k) acc = fmaf(w5t[k][i], win[t + k][i], acc);
-        acc = fminf(fmaxf(acc, -a.clip), a.clip);
-        cv[t][g][i] = acc;
-        if (t == 0) ss0 = fmaf(acc, acc, ss0);
-        else ss1 = fmaf(acc, acc, ss1);
+        for (int i = 0; i < 8; ++i) win[4 + t][i] = bf16_round(__fdividef(av[i], 1.0f + __expf(-bv[i])));  // GLU
+        store8_bf16(a.ring + rb + static_cast<size_t>((m.pos + 4 + t) & (kConvRing - 1)) * d + e0, win[4 + t]);
       }
+      float w5t[5][8];  // tap-major weights: 2 vector loads per tap
+#pragma unroll
+      for (int k = 0; k < 5; ++k) load8_nc(a.dw + static_cast<size_t>(k) * d + e0, w5t[k]);
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          float acc = 0.f;
+#pragma unroll
+          for (int k = 0; k < 5; ++k) acc = fmaf(w5t[k][i], win[t + k][i], acc);
+          acc = fminf(fmaxf(acc, -a.clip), a.clip);
+          cv[t][gg][i] = acc;
+          if (t == 0) ss0 = fmaf(acc, acc, ss0);
+          else ss1 = fmaf(acc, acc, ss1);
+        }
+    }
   }
-  const float r0 = rsqrtf(warp_sum(ss0) / static_cast<float>(d) + a.eps);
-  const float r1 = rsqrtf(warp_sum(ss1) / static_cast<float>(d) + a.eps);
+  ss0 = warp_sum(ss0);
+  ss1 = warp_sum(ss1);
+  if (W > 1) {
+    if (lane == 0) part[warp] = make_float2(ss0, ss1);
+    __syncthreads();
+    ss0 = ss1 = 0.f;
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    const int e0 = (g * 32 + lane) * 8;
+    for (int k = 0; k < W; ++k) {
+      const float2 v = part[sess * W + k];
+      ss0 += v.x;
+      ss1 += v.y;
+    }
+  }
+  if (!live) return;
+  const float r0 = rsqrtf(ss0 / static_cast<float>(d) + a.eps);
+  const float r1 = rsqrtf(ss1 / static_cast<float>(d) + a.eps);
+#pragma unroll
+  for (int gg = 0; gg < GW; ++gg) {
+    const int e0 = ((w * GW + gg) * 32 + lane) * 8;
     float wv[8];
     load8_nc(a.norm_w + e0, wv);
 #pragma unroll
@@ -325,7 +349,7 @@ __global__ void __launch_bounds__(128) lconv_kernel(LconvDev a) {
       float o[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i)
-        o[i] = fminf(fmaxf(silu_f(cv[t][g][i] * (t == 0 ? r0 : r1) * wv[i]), a.in_lo), a.in_hi);
+        o[i] = fminf(fmaxf(silu_f(cv[t][gg][i] * (t == 0 ? r0 : r1) * wv[i]), a.in_lo), a.in_hi);
       store8_act(a.xa + (static_cast<size_t>(row) * 2 + t) * d + e0, o, a.f16);
     }
   }
@@ -486,15 +510,18 @@ cudaError_t launch_lconv(Ctx& c, int layer, int rows_cap, cudaStream_t s) {
   a.in_lo = c.w.layers[layer].clip[7][0];  // linear_end input bounds
   a.in_hi = c.w.layers[layer].clip[7][1];
   a.f16 = c.weight_int8 != 0;
-  const int grid = (rows_cap + 3) / 4;  // 4 warps (sessions) per CTA
-  switch (c.cfg.hidden / 256) {
-    case 1: lconv_kernel<1><<<grid, 128, 0, s>>>(a); break;
-    case 2: lconv_kernel<2><<<grid, 128, 0, s>>>(a); break;
-    case 3: lconv_kernel<3><<<grid, 128, 0, s>>>(a); break;
-    case 4: lconv_kernel<4><<<grid, 128, 0, s>>>(a); break;
-    case 5: lconv_kernel<5><<<grid, 128, 0, s>>>(a); break;
-    case 6: lconv_kernel<6><<<grid, 128, 0, s>>>(a); break;
-    case 8: lconv_kernel<8><<<grid, 128, 0, s>>>(a); break;
+  // 256-thread CTAs: 8 sessions of one warp (odd G) or 4 sessions of two warps (even G)
+  const int g = c.cfg.hidden / 256;
+  const int per_cta = g % 2 == 0 ? 4 : 8;
+  const int grid = (rows_cap + per_cta - 1) / per_cta;
+  switch (g) {
+    case 1: lconv_kernel<1, 1><<<grid, 256, 0, s>>>(a); break;
+    case 2: lconv_kernel<2, 2><<<grid, 256, 0, s>>>(a); break;
+    case 3: lconv_kernel<3, 1><<<grid, 256, 0, s>>>(a); break;
+    case 4: lconv_kernel<4, 2><<<grid, 256, 0, s>>>(a); break;
+    case 5: lconv_kernel<5, 1><<<grid, 256, 0, s>>>(a); break;
+    case 6: lconv_kernel<6, 2><<<grid, 256, 0, s>>>(a); break;
+    case 8: lconv_kernel<8, 2><<<grid, 256, 0, s>>>(a); break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();
