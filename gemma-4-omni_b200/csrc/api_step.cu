@@ -27,10 +27,17 @@ struct lb_ctx {
     bool built = false;
     lb::GemmOp in_proj, out_proj, embed, qdown, rdown, film, fout;
     std::vector<LayerOps> layers;
-    cudaGraphExec_t graph[4] = {nullptr, nullptr, nullptr, nullptr};
-    int graph_kernels[4] = {0, 0, 0, 0};
+    // graph[0], graph[1]: the tower (PCM / mel input) through the soft tokens;
+    // graph[2]: the FiLM chain, launched after the query has landed
+    cudaGraphExec_t graph[3] = {nullptr, nullptr, nullptr};
+    int graph_kernels[3] = {0, 0, 0};
   };
   int last_graph_kernels = 0;
+  // side stream for the copies that need not sit on the step's critical path
+  // (query H2D under the tower, soft/raw D2H under FiLM), joined back into the
+  // caller's stream at the end of every step
+  cudaStream_t copy_stream = nullptr;
+  cudaEvent_t ev_begin = nullptr, ev_query = nullptr, ev_tower = nullptr, ev_copies = nullptr;
   std::vector<Plans> plans;
   // pinned staging for lb_step_host
   void* pinned = nullptr;
@@ -510,7 +517,8 @@ int build_plans(lb_ctx* x, int bi) {
     if (_e != cudaSuccess) return _e;        \
   } while (0)
 
-cudaError_t run_step(lb_ctx* x, int bi, int input_kind, bool film, cudaStream_t s) {
+// The tower: frontend, Conformer, output projection and embedder (soft tokens).
+cudaError_t run_tower(lb_ctx* x, int bi, int input_kind, cudaStream_t s) {
   Ctx& c = x->c;
   lb_ctx::Plans& P = x->plans[bi];
   const Bucket& b = c.buckets[bi];
@@ -613,16 +621,51 @@ cudaError_t run_step(lb_ctx* x, int bi, int input_kind, bool film, cudaStream_t 
   LB_TRY(launch_outputs(c, tc, 0, s));
   LB_TRY(run_op(c, P.embed, tc, nullptr, s));
   LB_TRY(launch_outputs(c, tc, 1, s));
-  if (film) {
-    LB_TRY(launch_film(c, tc, 0, s));
-    LB_TRY(run_op(c, P.qdown, tc, nullptr, s));
-    LB_TRY(run_op(c, P.rdown, tc, c.film_rd_bf, s));
-    LB_TRY(run_op(c, P.film, tc, nullptr, s));
-    LB_TRY(launch_film(c, tc, 1, s));
-    LB_TRY(run_op(c, P.fout, tc, nullptr, s));
-    LB_TRY(launch_film(c, tc, 2, s));
-  }
   return cudaSuccess;
+}
+
+// The FiLM adapter over the soft tokens and the query.
+cudaError_t run_film(lb_ctx* x, int bi, cudaStream_t s) {
+  Ctx& c = x->c;
+  lb_ctx::Plans& P = x->plans[bi];
+  const int tc = c.buckets[bi].tok_cap;
+  LB_TRY(launch_film(c, tc, 0, s));
+  LB_TRY(run_op(c, P.qdown, tc, nullptr, s));
+  LB_TRY(run_op(c, P.rdown, tc, c.film_rd_bf, s));
+  LB_TRY(run_op(c, P.film, tc, nullptr, s));
+  LB_TRY(launch_film(c, tc, 1, s));
+  LB_TRY(run_op(c, P.fout, tc, nullptr, s));
+  LB_TRY(launch_film(c, tc, 2, s));
+  return cudaSuccess;
+}
+
+// Captures `part` (0/1: the tower for that input kind, 2: FiLM) of bucket bi once.
+int ensure_graph(lb_ctx* x, int bi, int part) {
+  Ctx& c = x->c;
+  lb_ctx::Plans& P = x->plans[bi];
+  if (P.graph[part]) return LB_OK;
+  cudaGraph_t graph = nullptr;
+  cudaError_t e = cudaStreamBeginCapture(c.capture_stream, cudaStreamCaptureModeThreadLocal);
+  if (e != cudaSuccess) return LB_ERR_CUDA;
+  cudaError_t e_run = part == 2 ? run_film(x, bi, c.capture_stream) : run_tower(x, bi, part, c.capture_stream);
+  e = cudaStreamEndCapture(c.capture_stream, &graph);
+  if (e_run != cudaSuccess || e != cudaSuccess) {
+    if (graph) cudaGraphDestroy(graph);
+    return LB_ERR_CUDA;
+  }
+  size_t num_nodes = 0;
+  cudaGraphGetNodes(graph, nullptr, &num_nodes);
+  std::vector<cudaGraphNode_t> nodes(num_nodes);
+  cudaGraphGetNodes(graph, nodes.data(), &num_nodes);
+  int kernels = 0;
+  for (auto nd : nodes) {
+    cudaGraphNodeType t;
+    if (cudaGraphNodeGetType(nd, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) ++kernels;
+  }
+  P.graph_kernels[part] = kernels;
+  e = cudaGraphInstantiate(&P.graph[part], graph, 0);
+  cudaGraphDestroy(graph);
+  return e == cudaSuccess ? LB_OK : LB_ERR_CUDA;
 }
 
 int pick_bucket(Ctx& c, int n) {
@@ -704,6 +747,9 @@ int lb_create(const lb_config* cfg, lb_ctx** out_ctx) {
   }
   x->plans.resize(c.buckets.size());
   cudaStreamCreateWithFlags(&c.capture_stream, cudaStreamNonBlocking);
+  if (cudaStreamCreateWithFlags(&x->copy_stream, cudaStreamNonBlocking) != cudaSuccess) return LB_ERR_CUDA;
+  for (cudaEvent_t* ev : {&x->ev_begin, &x->ev_query, &x->ev_tower, &x->ev_copies})
+    if (cudaEventCreateWithFlags(ev, cudaEventDisableTiming) != cudaSuccess) return LB_ERR_CUDA;
   x->pinned_bytes = static_cast<size_t>(cfg->max_rows) *
                     (4 + 8 * 3 + 1 + kPcm * 4 + 2 * (cfg->film_query_dim + cfg->output_dims +
                                                       cfg->text_hidden + cfg->film_query_dim) * 2) +
@@ -724,6 +770,9 @@ int lb_destroy(lb_ctx* x) {
     for (auto& gph : p.graph)
       if (gph) cudaGraphExecDestroy(gph);
   if (c.capture_stream) cudaStreamDestroy(c.capture_stream);
+  if (x->copy_stream) cudaStreamDestroy(x->copy_stream);
+  for (cudaEvent_t ev : {x->ev_begin, x->ev_query, x->ev_tower, x->ev_copies})
+    if (ev) cudaEventDestroy(ev);
   if (x->pinned) cudaFreeHost(x->pinned);
   cudaFree(c.weight_arena);
   if (c.wide_arena) cudaFree(c.wide_arena);
@@ -886,8 +935,21 @@ int lb_set_debug_outputs(lb_ctx* x, float* subsampled, float* layers) {
   return LB_OK;
 }
 
+namespace {
+int step_enqueue(lb_ctx* x, int kind, const void* input, const void* query, void* out_raw, void* out_soft,
+                 void* out_film, void* stream, bool overlap);
+}
+
 int lb_step_async(lb_ctx* x, int kind, const void* input, const void* query, void* out_raw,
                   void* out_soft, void* out_film, void* stream) {
+  return step_enqueue(x, kind, input, query, out_raw, out_soft, out_film, stream, false);
+}
+
+namespace {
+// overlap: the query H2D and the raw/soft D2H run on the context's copy stream
+// under the compute (host buffers); otherwise every copy stays on `stream`.
+int step_enqueue(lb_ctx* x, int kind, const void* input, const void* query, void* out_raw, void* out_soft,
+                 void* out_film, void* stream, bool overlap) {
   if (!x || !input) return LB_ERR_INVALID_ARGUMENT;
   Ctx& c = x->c;
   if (c.state != 1) return LB_ERR_STATE;
@@ -902,56 +964,62 @@ int lb_step_async(lb_ctx* x, int kind, const void* input, const void* query, voi
   if (bi < 0) return LB_ERR_CAPACITY;
   int rc = build_plans(x, bi);
   if (rc) return rc;
-  cudaError_t e;
-  if (kind == LB_INPUT_PCM) e = cudaMemcpyAsync(c.in_pcm, input, 4ull * n * kPcm, cudaMemcpyDefault, s);
-  else e = cudaMemcpyAsync(c.in_mel, input, 4ull * n * 8 * kMelBins, cudaMemcpyDefault, s);
-  if (e == cudaSuccess && film)
-    e = cudaMemcpyAsync(c.in_query, query, 2ull * n * 2 * c.cfg.film_query_dim, cudaMemcpyDefault, s);
+  // The query is only read by FiLM after the tower, so its H2D runs on the
+  // context's copy stream meanwhile (ordered after everything the caller
+  // enqueued before this step, the previous step's FiLM included); the raw and
+  // soft tokens are final once the tower ends, so their D2H overlaps FiLM.
+  // The copy stream is joined back into `s` at the end of the step.
+  cudaStream_t cs = overlap ? x->copy_stream : s;
+  cudaError_t e = cudaSuccess;
+  if (overlap) {
+    e = cudaEventRecord(x->ev_begin, s);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(cs, x->ev_begin, 0);
+  }
+  if (e == cudaSuccess && film) {
+    e = cudaMemcpyAsync(c.in_query, query, 2ull * n * 2 * c.cfg.film_query_dim, cudaMemcpyDefault, cs);
+    if (e == cudaSuccess && overlap) e = cudaEventRecord(x->ev_query, cs);
+  }
+  if (e == cudaSuccess) {
+    if (kind == LB_INPUT_PCM) e = cudaMemcpyAsync(c.in_pcm, input, 4ull * n * kPcm, cudaMemcpyDefault, s);
+    else e = cudaMemcpyAsync(c.in_mel, input, 4ull * n * 8 * kMelBins, cudaMemcpyDefault, s);
+  }
   if (e != cudaSuccess) return LB_ERR_CUDA;
   const bool eager = c.dbg_sub || c.dbg_layers || c.dbg_stop_layer >= 0;
   lb_ctx::Plans& P = x->plans[bi];
-  const int variant = kind * 2 + (film ? 1 : 0);
   if (eager) {
-    e = run_step(x, bi, kind, film, s);
+    e = run_tower(x, bi, kind, s);
   } else {
-    if (!P.graph[variant]) {
-      cudaGraph_t graph = nullptr;
-      e = cudaStreamBeginCapture(c.capture_stream, cudaStreamCaptureModeThreadLocal);
-      if (e != cudaSuccess) return LB_ERR_CUDA;
-      cudaError_t e_run = run_step(x, bi, kind, film, c.capture_stream);
-      e = cudaStreamEndCapture(c.capture_stream, &graph);
-      if (e_run != cudaSuccess || e != cudaSuccess) {
-        if (graph) cudaGraphDestroy(graph);
-        return LB_ERR_CUDA;
-      }
-      size_t num_nodes = 0;
-      cudaGraphGetNodes(graph, nullptr, &num_nodes);
-      std::vector<cudaGraphNode_t> nodes(num_nodes);
-      cudaGraphGetNodes(graph, nodes.data(), &num_nodes);
-      int kernels = 0;
-      for (auto nd : nodes) {
-        cudaGraphNodeType t;
-        if (cudaGraphNodeGetType(nd, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) ++kernels;
-      }
-      P.graph_kernels[variant] = kernels;
-      e = cudaGraphInstantiate(&P.graph[variant], graph, 0);
-      cudaGraphDestroy(graph);
-      if (e != cudaSuccess) return LB_ERR_CUDA;
-    }
-    x->last_graph_kernels = P.graph_kernels[variant];
-    e = cudaGraphLaunch(P.graph[variant], s);
+    rc = ensure_graph(x, bi, kind);
+    if (rc == LB_OK && film) rc = ensure_graph(x, bi, 2);
+    if (rc) return rc;
+    x->last_graph_kernels = P.graph_kernels[kind] + (film ? P.graph_kernels[2] : 0);
+    e = cudaGraphLaunch(P.graph[kind], s);
   }
   if (e != cudaSuccess) return LB_ERR_CUDA;
   const size_t toks = 2ull * n;
-  if (out_raw) e = cudaMemcpyAsync(out_raw, c.out_raw, toks * c.cfg.output_dims * 2, cudaMemcpyDefault, s);
+  if (overlap) {
+    e = cudaEventRecord(x->ev_tower, s);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(cs, x->ev_tower, 0);
+  }
+  if (e == cudaSuccess && out_raw)
+    e = cudaMemcpyAsync(out_raw, c.out_raw, toks * c.cfg.output_dims * 2, cudaMemcpyDefault, cs);
   if (e == cudaSuccess && out_soft)
-    e = cudaMemcpyAsync(out_soft, c.out_soft, toks * c.cfg.text_hidden * 2, cudaMemcpyDefault, s);
-  if (e == cudaSuccess && out_film)
-    e = cudaMemcpyAsync(out_film, c.out_film, toks * c.cfg.film_query_dim * 2, cudaMemcpyDefault, s);
+    e = cudaMemcpyAsync(out_soft, c.out_soft, toks * c.cfg.text_hidden * 2, cudaMemcpyDefault, cs);
+  if (e == cudaSuccess && film) {
+    if (overlap) e = cudaStreamWaitEvent(s, x->ev_query, 0);
+    if (e == cudaSuccess) e = eager ? run_film(x, bi, s) : cudaGraphLaunch(P.graph[2], s);
+    if (e == cudaSuccess && out_film)
+      e = cudaMemcpyAsync(out_film, c.out_film, toks * c.cfg.film_query_dim * 2, cudaMemcpyDefault, s);
+  }
+  if (e == cudaSuccess && overlap) {
+    e = cudaEventRecord(x->ev_copies, cs);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(s, x->ev_copies, 0);
+  }
   if (e != cudaSuccess) return LB_ERR_CUDA;
   c.state = 2;
   return LB_OK;
 }
+}  // namespace
 
 int lb_commit_async(lb_ctx* x, void* stream) {
   if (!x) return LB_ERR_INVALID_ARGUMENT;
@@ -1136,8 +1204,8 @@ int lb_step_host(lb_ctx* x, int n, const int32_t* handles, const int64_t* keys, 
                          static_cast<int64_t*>(pf), static_cast<int64_t*>(pq),
                          static_cast<uint8_t*>(pm), stream);
   if (rc) return rc;
-  rc = lb_step_async(x, kind, pin, pqry, out_raw ? o_raw : nullptr, out_soft ? o_soft : nullptr,
-                     out_film ? o_film : nullptr, stream);
+  rc = step_enqueue(x, kind, pin, pqry, out_raw ? o_raw : nullptr, out_soft ? o_soft : nullptr,
+                    out_film ? o_film : nullptr, stream, true);
   if (rc) return rc;
   if (commit) {
     rc = lb_commit_async(x, stream);
