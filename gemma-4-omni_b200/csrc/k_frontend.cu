@@ -126,7 +126,7 @@ __global__ void __launch_bounds__(256) mel_kernel(MelArgs a) {
 
 // ------------------------------------------------------------ subsampler
 constexpr int kF0 = 64;        // conv0 output frequencies
-constexpr int kCiPad = 132;    // channel stride of the conv1 input tile (bank-conflict free)
+constexpr int kCiPad = 136;    // channel stride of the conv1 input tile (16-byte rows for ldmatrix)
 constexpr int kK1 = 9 * 128;   // conv1 reduction length
 constexpr int kK1Pad = kK1 + 8;
 constexpr int kSubThreads = 256;
@@ -163,6 +163,13 @@ __device__ __forceinline__ void mma_f16_16816(float (&d)[4], uint32_t a0, uint32
       "{%8,%9}, {%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr)
+               : "memory");
 }
 
 __device__ __forceinline__ uint32_t pack_f16x2(float x, float y) {
@@ -358,25 +365,24 @@ __global__ void __launch_bounds__(kSubThreads, 1) subsample_kernel(SubArgs a) {
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
       const int p_lo = pt * 16 + g, p_hi = p_lo + 8;
-      const int t_lo = p_lo >> 5, f_lo = p_lo & 31, t_hi = p_hi >> 5, f_hi = p_hi & 31;
+      // ldmatrix.x4 row addresses: lane L feeds row L%8 of matrix L/8.  A: the
+      // 16 positions of this tile (matrices 0/1: positions +0..7 / +8..15 at
+      // k 0..7, matrices 2/3: the same at k 8..15); B: output channels
+      // ch*16 + 0..7 (matrices 0/1: k 0..7 / 8..15) and + 8..15 (matrices 2/3).
+      // Per k-step only the tap / channel-chunk offset changes (an immediate).
+      const int mi = lane >> 3, mr = lane & 7;
+      const int pa = pt * 16 + mr + (mi & 1) * 8;
+      const uint32_t a_lane = smem_u32(xin + ((2 * (pa >> 5)) * 66 + 2 * (pa & 31)) * kCiPad + (mi >> 1) * 8);
+      const uint32_t b_lane = smem_u32(w1s + (ch * 16 + (mi >> 1) * 8 + mr) * kK1Pad + (mi & 1) * 8);
+#pragma unroll
       for (int ks = 0; ks < kK1 / 16; ++ks) {
         const int tap = ks >> 3, ci0 = (ks & 7) * 16;
         const int i = tap / 3, j = tap % 3;
-        const __nv_bfloat16* rlo = xin + ((2 * t_lo + i) * 66 + 2 * f_lo + j) * kCiPad + ci0;
-        const __nv_bfloat16* rhi = xin + ((2 * t_hi + i) * 66 + 2 * f_hi + j) * kCiPad + ci0;
-        uint32_t af[4];
-        af[0] = *reinterpret_cast<const uint32_t*>(rlo + 2 * tq);
-        af[1] = *reinterpret_cast<const uint32_t*>(rhi + 2 * tq);
-        af[2] = *reinterpret_cast<const uint32_t*>(rlo + 2 * tq + 8);
-        af[3] = *reinterpret_cast<const uint32_t*>(rhi + 2 * tq + 8);
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-          const int co = ch * 16 + nt * 8 + g;
-          const __nv_bfloat16* wb = w1s + co * kK1Pad + ks * 16;
-          const uint32_t b0 = *reinterpret_cast<const uint32_t*>(wb + 2 * tq);
-          const uint32_t b1 = *reinterpret_cast<const uint32_t*>(wb + 2 * tq + 8);
-          mma_bf16_16816(acc[nt], af, b0, b1);
-        }
+        uint32_t af[4], bf[4];
+        ldsm_x4(a_lane + ((i * 66 + j) * kCiPad + ci0) * 2, af[0], af[1], af[2], af[3]);
+        ldsm_x4(b_lane + ks * 32, bf[0], bf[1], bf[2], bf[3]);
+        mma_bf16_16816(acc[0], af, bf[0], bf[1]);
+        mma_bf16_16816(acc[1], af, bf[2], bf[3]);
       }
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt) {

@@ -83,55 +83,6 @@ __device__ __forceinline__ void store8_bf16(__nv_bfloat16* p, const float (&v)[8
   *reinterpret_cast<int4*>(p) = r;
 }
 
-// Two block sums at once (one set of barriers); sh holds >= 64 floats.
-__device__ __forceinline__ float2 block_sum2(float2 v, float* sh) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  v.x = warp_sum(v.x);
-  v.y = warp_sum(v.y);
-  __syncthreads();
-  if (lane == 0) {
-    sh[warp] = v.x;
-    sh[32 + warp] = v.y;
-  }
-  __syncthreads();
-  float2 t = make_float2(0.f, 0.f);
-  for (int i = 0; i < nw; ++i) {
-    t.x += sh[i];
-    t.y += sh[32 + i];
-  }
-  return t;
-}
-
-// RMSNorm of the same 8-element slice of two rows, weights in registers.
-__device__ __forceinline__ void rms8w2(float (&v0)[8], float (&v1)[8], const float (&w8)[8], int d, float eps,
-                                       float* sh) {
-  float2 ss = make_float2(0.f, 0.f);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    ss.x = fmaf(v0[i], v0[i], ss.x);
-    ss.y = fmaf(v1[i], v1[i], ss.y);
-  }
-  ss = block_sum2(ss, sh);
-  const float r0 = rsqrtf(ss.x / static_cast<float>(d) + eps);
-  const float r1 = rsqrtf(ss.y / static_cast<float>(d) + eps);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    v0[i] = v0[i] * r0 * w8[i];
-    v1[i] = v1[i] * r1 * w8[i];
-  }
-}
-
-// RMSNorm with the weights already in registers (w8: this thread's 8 weights).
-__device__ __forceinline__ void rms8w(float (&v)[8], const float (&w8)[8], int d, float eps, float* sh) {
-  float ss = 0.f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) ss += v[i] * v[i];
-  ss = block_sum(ss, sh);
-  const float r = rsqrtf(ss / static_cast<float>(d) + eps);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) v[i] = v[i] * r * w8[i];
-}
-
 // RMSNorm of 8-element thread slices over a block row: x * pow(mean(x^2)+eps, -0.5) * w
 __device__ __forceinline__ void rms8(float (&v)[8], const float* w, int e0, int d, float eps,
                                      float* sh) {
@@ -169,76 +120,96 @@ struct RowFusedDev {
   bool f16;  // xa holds fp16 (int8-weight GEMM input) instead of bf16
 };
 
-// One CTA of d/8 threads per session row, i.e. both tick tokens (the live token
-// count is always even), 8 contiguous elements of each token per thread; the
-// two tokens' norms share their block reductions.  Half as many CTAs as
-// tokens keeps a 2048-token step within one wave of resident CTAs.
-__global__ void __launch_bounds__(256) row_fused_kernel(RowFusedDev a) {
-  __shared__ float sh[64];
-  const int t0 = 2 * blockIdx.x;
-  const int e0 = threadIdx.x * 8;
-  const size_t base0 = static_cast<size_t>(t0) * a.d + e0, base1 = base0 + a.d;
-  // every input is requested up front, together with the live token count: the
-  // rows (in bounds for every token of the bucket), the GEMM outputs and the
-  // (read only) norm weights -- one memory round trip before the stores
+// One warp per token: lane owns G groups of 8 elements, e = (g*32 + lane)*8,
+// so each load is a whole-warp coalesced 512-byte run and every RMS reduction
+// is five shuffles (no block barriers).  All 2G 32-byte loads of h and y are
+// in flight together; at ~128 registers a thread, 16 warps fit per SM, i.e. a
+// 2048-token step in one wave.
+template <int G>
+__global__ void __launch_bounds__(128, 4) row_fused_kernel(RowFusedDev a) {
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 4 + (threadIdx.x >> 5);  // the grid covers the bucket's tokens exactly
+  constexpr int d = G * 256;
+  constexpr float inv_d = 1.0f / static_cast<float>(d);
+  const size_t base = static_cast<size_t>(t) * d + lane * 8;
   const int n_tok = a.counts[1];
-  float h0[8], h1[8], y0[8], y1[8], pw[8], ow[8], qw[8];
-  load8(a.h + base0, h0);
-  load8(a.h + base1, h1);
-  if (a.y) {
-    load8(a.y + base0, y0);
-    load8(a.y + base1, y1);
-  }
+  float h[G][8], y[G][8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) pw[i] = ow[i] = qw[i] = 1.0f;
-  if (a.post_w) load8_nc(a.post_w + e0, pw);
-  if (a.out_w) load8_nc(a.out_w + e0, ow);
-  if (a.xa && a.pre_norm && a.pre_w) load8_nc(a.pre_w + e0, qw);
-  if (t0 >= n_tok) return;
+  for (int g = 0; g < G; ++g) {
+    load8(a.h + base + g * 256, h[g]);
+    if (a.y) load8(a.y + base + g * 256, y[g]);
+  }
+  if (t >= n_tok) return;
   if (a.y) {
     if (a.post_w) {
+      float ss = 0.f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        y0[i] = fminf(fmaxf(y0[i], -a.clip), a.clip);
-        y1[i] = fminf(fmaxf(y1[i], -a.clip), a.clip);
+      for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          y[g][i] = fminf(fmaxf(y[g][i], -a.clip), a.clip);
+          ss = fmaf(y[g][i], y[g][i], ss);
+        }
+      const float r = rsqrtf(warp_sum(ss) * inv_d + a.eps);
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float w8[8];
+        load8_nc(a.post_w + lane * 8 + g * 256, w8);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) y[g][i] = y[g][i] * r * w8[i];
       }
-      rms8w2(y0, y1, pw, a.d, a.eps, sh);
     }
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      h0[i] = a.residual ? fmaf(y0[i], a.alpha, h0[i]) : y0[i] * a.alpha;
-      h1[i] = a.residual ? fmaf(y1[i], a.alpha, h1[i]) : y1[i] * a.alpha;
-    }
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) h[g][i] = a.residual ? fmaf(y[g][i], a.alpha, h[g][i]) : y[g][i] * a.alpha;
   }
   if (a.out_w) {
+    float ss = 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      h0[i] = fminf(fmaxf(h0[i], -a.clip), a.clip);
-      h1[i] = fminf(fmaxf(h1[i], -a.clip), a.clip);
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        h[g][i] = fminf(fmaxf(h[g][i], -a.clip), a.clip);
+        ss = fmaf(h[g][i], h[g][i], ss);
+      }
+    const float r = rsqrtf(warp_sum(ss) * inv_d + a.eps);
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float w8[8];
+      load8_nc(a.out_w + lane * 8 + g * 256, w8);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) h[g][i] = h[g][i] * r * w8[i];
     }
-    rms8w2(h0, h1, ow, a.d, a.eps, sh);
   }
-  store8(a.h + base0, h0);
-  store8(a.h + base1, h1);
-  if (a.dbg) {
-    store8(a.dbg + base0, h0);
-    store8(a.dbg + base1, h1);
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    store8(a.h + base + g * 256, h[g]);
+    if (a.dbg) store8(a.dbg + base + g * 256, h[g]);
   }
   if (a.xa) {
-    float x0[8], x1[8];
+    float ss = 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      x0[i] = a.pre_clamp ? fminf(fmaxf(h0[i], -a.clip), a.clip) : h0[i];
-      x1[i] = a.pre_clamp ? fminf(fmaxf(h1[i], -a.clip), a.clip) : h1[i];
-    }
-    if (a.pre_norm) rms8w2(x0, x1, qw, a.d, a.eps, sh);
+    for (int g = 0; g < G; ++g)
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      x0[i] = fminf(fmaxf(x0[i], a.in_lo), a.in_hi);
-      x1[i] = fminf(fmaxf(x1[i], a.in_lo), a.in_hi);
+      for (int i = 0; i < 8; ++i) {
+        if (a.pre_clamp) h[g][i] = fminf(fmaxf(h[g][i], -a.clip), a.clip);
+        ss = fmaf(h[g][i], h[g][i], ss);
+      }
+    const float r = a.pre_norm ? rsqrtf(warp_sum(ss) * inv_d + a.eps) : 1.0f;
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float w8[8];
+      if (a.pre_norm && a.pre_w) {
+        load8_nc(a.pre_w + lane * 8 + g * 256, w8);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) w8[i] = 1.0f;
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) h[g][i] = fminf(fmaxf(h[g][i] * r * w8[i], a.in_lo), a.in_hi);
+      store8_act(a.xa + base + g * 256, h[g], a.f16);
     }
-    store8_act(a.xa + base0, x0, a.f16);
-    store8_act(a.xa + base1, x1, a.f16);
   }
 }
 
@@ -486,7 +457,17 @@ cudaError_t launch_row_fused(Ctx& c, int tok_cap, const RowFusedArgs& r, cudaStr
   a.xa = r.xa;
   a.dbg = r.dbg;
   a.f16 = c.weight_int8 != 0;
-  row_fused_kernel<<<tok_cap / 2, c.cfg.hidden / 8, 0, s>>>(a);  // one CTA per session (2 tokens)
+  const int grid = tok_cap / 4;  // four tokens (warps) per CTA; tok_cap is a multiple of 32
+  switch (c.cfg.hidden / 256) {
+    case 1: row_fused_kernel<1><<<grid, 128, 0, s>>>(a); break;
+    case 2: row_fused_kernel<2><<<grid, 128, 0, s>>>(a); break;
+    case 3: row_fused_kernel<3><<<grid, 128, 0, s>>>(a); break;
+    case 4: row_fused_kernel<4><<<grid, 128, 0, s>>>(a); break;
+    case 5: row_fused_kernel<5><<<grid, 128, 0, s>>>(a); break;
+    case 6: row_fused_kernel<6><<<grid, 128, 0, s>>>(a); break;
+    case 8: row_fused_kernel<8><<<grid, 128, 0, s>>>(a); break;
+    default: return cudaErrorInvalidValue;
+  }
   return cudaGetLastError();
 }
 
