@@ -144,7 +144,10 @@ int lb_step_async(lb_ctx* ctx, int input_kind, const void* input, const void* qu
  * outputs back and synchronises the stream before returning (end-to-end
  * form of one serving tick).  Row arrays as in lb_pack_async, host memory.
  * Page-locked (pinned) buffers are transferred by DMA directly; pageable ones
- * pass through the context's pinned staging area (one extra host copy). */
+ * pass through the context's pinned staging area (one extra host copy).  The
+ * FiLM query is copied in on a context-owned copy stream while the tower runs,
+ * and raw/soft tokens are copied out on it while FiLM runs; that stream is
+ * joined back into `stream` before the call returns. */
 int lb_step_host(lb_ctx* ctx, int n_rows, const int32_t* handles, const int64_t* keys,
                  const int64_t* frames, const int64_t* seqs, const uint8_t* masks,
                  int input_kind, const void* input, const void* query, void* out_raw,
