@@ -39,17 +39,76 @@ struct MelArgs {
   const int2* filter_range;                          // [128] (k_lo, k_hi)
 };
 
+// One complex multiply-free radix-4 DFT in place: (x0, x1, x2, x3) ->
+// (X0, X1, X2, X3) with W4 = exp(-2 pi i / 4) = -i.
+__device__ __forceinline__ void dft4(float& r0, float& i0, float& r1, float& i1, float& r2, float& i2, float& r3,
+                                     float& i3) {
+  const float t0r = r0 + r2, t0i = i0 + i2, t1r = r0 - r2, t1i = i0 - i2;
+  const float t2r = r1 + r3, t2i = i1 + i3, t3r = r1 - r3, t3i = i1 - i3;
+  r0 = t0r + t2r;
+  i0 = t0i + t2i;
+  r2 = t0r - t2r;
+  i2 = t0i - t2i;
+  r1 = t1r + t3i;  // t1 - i t3
+  i1 = t1i - t3r;
+  r3 = t1r - t3i;  // t1 + i t3
+  i3 = t1i + t3r;
+}
+
+// 16-point DFT in registers, natural order in and out, as 4 x 4: radix-4 DFTs
+// over n1 of x[4 n1 + n2], twiddles W16^(n2 k1), radix-4 DFTs over n2.
+// Twiddles W16^j = W512^(32 j) come from the exact 512-entry table.
+__device__ __forceinline__ void dft16(float (&re)[16], float (&im)[16], const float* __restrict__ ct,
+                                      const float* __restrict__ st) {
+#pragma unroll
+  for (int n2 = 0; n2 < 4; ++n2) dft4(re[n2], im[n2], re[4 + n2], im[4 + n2], re[8 + n2], im[8 + n2], re[12 + n2], im[12 + n2]);
+  // element 4 k1 + n2 now holds A[n2][k1]
+#pragma unroll
+  for (int n2 = 1; n2 < 4; ++n2)
+#pragma unroll
+    for (int k1 = 1; k1 < 4; ++k1) {
+      const int j = n2 * k1;  // 1..9
+      const float wr = __ldg(ct + 32 * j), wi = -__ldg(st + 32 * j);
+      const float ar = re[4 * k1 + n2], ai = im[4 * k1 + n2];
+      re[4 * k1 + n2] = ar * wr - ai * wi;
+      im[4 * k1 + n2] = ar * wi + ai * wr;
+    }
+  float orr[16], oi[16];
+#pragma unroll
+  for (int k1 = 0; k1 < 4; ++k1) {
+    float a0 = re[4 * k1], b0 = im[4 * k1], a1 = re[4 * k1 + 1], b1 = im[4 * k1 + 1];
+    float a2 = re[4 * k1 + 2], b2 = im[4 * k1 + 2], a3 = re[4 * k1 + 3], b3 = im[4 * k1 + 3];
+    dft4(a0, b0, a1, b1, a2, b2, a3, b3);  // over n2 -> k2
+    orr[k1] = a0, oi[k1] = b0;
+    orr[k1 + 4] = a1, oi[k1 + 4] = b1;
+    orr[k1 + 8] = a2, oi[k1 + 8] = b2;
+    orr[k1 + 12] = a3, oi[k1 + 12] = b3;
+  }
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    re[k] = orr[k];
+    im[k] = oi[k];
+  }
+}
+
 // |X[k]|, k = 0..256, of the 512-point real DFT of each frame (zero-padded from
 // 320 samples), computed as a 256-point complex FFT of z[m] = x[2m] + i x[2m+1]
 // followed by the real-input split X[k] = E[k] + W^k O[k] with
 // E = (Z[k] + conj Z[256-k]) / 2, O = (Z[k] - conj Z[256-k]) / 2i and
-// W = exp(-2 pi i / 512).  Radix-2 decimation in time, bit-reversed input,
-// exact twiddles cos/sin(2 pi j / 512) from the table; fp32 throughout.
+// W = exp(-2 pi i / 512).  The 256-point FFT is the four-step 16 x 16 form:
+// with m = 16 a + b and k = k1 + 16 k2,
+//   Z[k1 + 16 k2] = sum_b W16^(b k2) W256^(b k1) sum_a z[16 a + b] W16^(a k1),
+// i.e. 16-point DFTs in registers (one thread per frame and column), a twiddle,
+// one padded shared-memory transpose, and 16-point DFTs again.  Exact twiddles
+// cos/sin(2 pi j / 512) from the table; fp32 throughout.
 __global__ void __launch_bounds__(256) mel_kernel(MelArgs a) {
   const int row = blockIdx.x;
-  __shared__ float zr[kFrames][256], zi[kFrames][256];
-  __shared__ float mag[kFrames][kBins + 3];
-  __shared__ float ct[512], st[512];
+  constexpr int kSig = kTail + kPcm;                // padded signal [tail | pcm]
+  __shared__ __align__(16) float sig[kSig];         // phases 0-1
+  __shared__ float yr[kFrames][16][17], yi[kFrames][16][17];  // after the first DFTs
+  __shared__ float zr[kFrames][256], zi[kFrames][256];        // natural-order spectrum
+  float (*mag)[kBins + 3] = reinterpret_cast<float (*)[kBins + 3]>(&yr[0][0][0]);  // reuses yr/yi
+  static_assert(sizeof(yr) + sizeof(yi) >= sizeof(float) * kFrames * (kBins + 3), "mag fits in yr/yi");
   // row tables (in bounds for every row of the bucket) read with the live count
   const int n_rows = a.counts[0];
   const int slot = a.row_slot[row];
@@ -60,62 +119,81 @@ __global__ void __launch_bounds__(256) mel_kernel(MelArgs a) {
   const bool fresh = reason == 3 || reason == 1;
   const float* tail_in = a.tail + (static_cast<size_t>(slot) * 2 + parity) * kTail;
   const float* pcm = a.pcm + static_cast<size_t>(row) * kPcm;
-  for (int i = threadIdx.x; i < 512; i += blockDim.x) {
-    ct[i] = a.cos_tab[i];
-    st[i] = a.sin_tab[i];
+  const int tid = threadIdx.x;
+  // ---- phase 0: [tail | pcm] into shared memory (16-byte loads), new tail out
+  for (int i = tid; i < kSig / 4; i += blockDim.x) {
+    float4 v;
+    if (i < kTail / 4) {
+      v = fresh ? make_float4(0.f, 0.f, 0.f, 0.f) : __ldg(reinterpret_cast<const float4*>(tail_in) + i);
+    } else {
+      v = __ldg(reinterpret_cast<const float4*>(pcm) + (i - kTail / 4));
+    }
+    reinterpret_cast<float4*>(sig)[i] = v;
   }
-  // frame f covers padded samples [160 f, 160 f + 320) of [tail | pcm | 0]; the
-  // windowed product is formed in fp32 as the reference's float32 NumPy does
-  auto sample = [&](int f, int n) {
-    if (n >= kWin) return 0.0f;
-    const int sidx = f * 160 + n;  // index into the padded signal (never the final pad sample)
-    const float v = sidx < kTail ? (fresh ? 0.0f : tail_in[sidx]) : pcm[sidx - kTail];
-    return v * a.window[n];
-  };
-  for (int i = threadIdx.x; i < kFrames * 256; i += blockDim.x) {
-    const int f = i >> 8, m = i & 255;
-    const int r = static_cast<int>(__brev(static_cast<unsigned>(m)) >> 24);
-    zr[f][r] = sample(f, 2 * m);
-    zi[f][r] = sample(f, 2 * m + 1);
+  float* tail_out = a.tail + (static_cast<size_t>(slot) * 2 + (parity ^ 1)) * kTail;
+  for (int i = tid; i < kTail / 4; i += blockDim.x)
+    reinterpret_cast<float4*>(tail_out)[i] = __ldg(reinterpret_cast<const float4*>(pcm) + (kPcm - kTail) / 4 + i);
+  __syncthreads();
+  // ---- phase 1: thread (f, b) -> Y[k1] = sum_a z[16 a + b] W16^(a k1), times
+  // W256^(b k1); z[m] = 0 for m >= 160 (samples past the 320-sample window).
+  // The windowed product is formed in fp32 as the reference's float32 NumPy does.
+  if (tid < kFrames * 16) {
+    const int f = tid >> 4, b = tid & 15;
+    float re[16], im[16];
+#pragma unroll
+    for (int q = 0; q < 16; ++q) {
+      if (q < 10) {
+        const int n = 32 * q + 2 * b;  // < 320
+        re[q] = sig[f * 160 + n] * __ldg(a.window + n);
+        im[q] = sig[f * 160 + n + 1] * __ldg(a.window + n + 1);
+      } else {
+        re[q] = 0.f;
+        im[q] = 0.f;
+      }
+    }
+    dft16(re, im, a.cos_tab, a.sin_tab);
+#pragma unroll
+    for (int k1 = 0; k1 < 16; ++k1) {
+      const int j = 2 * b * k1;  // W256^(b k1) = W512^(2 b k1), 2 b k1 <= 450
+      const float wr = __ldg(a.cos_tab + j), wi = -__ldg(a.sin_tab + j);
+      yr[f][k1][b] = re[k1] * wr - im[k1] * wi;
+      yi[f][k1][b] = re[k1] * wi + im[k1] * wr;
+    }
   }
   __syncthreads();
-  // staged tail for the next tick: last 160 PCM samples
-  float* tail_out = a.tail + (static_cast<size_t>(slot) * 2 + (parity ^ 1)) * kTail;
-  for (int i = threadIdx.x; i < kTail; i += blockDim.x) tail_out[i] = pcm[kPcm - kTail + i];
-  // 256-point complex FFT of every frame, 8 stages
-  for (int len = 2, tstep = 256; len <= 256; len <<= 1, tstep >>= 1) {
-    const int half = len >> 1;
-    for (int b = threadIdx.x; b < kFrames * 128; b += blockDim.x) {
-      const int f = b >> 7, j = b & 127;
-      const int pos = j & (half - 1);
-      const int i0 = (j - pos) * 2 + pos, i1 = i0 + half;
-      const float wr = ct[pos * tstep], wi = -st[pos * tstep];  // exp(-2 pi i pos / len)
-      const float br = zr[f][i1], bi = zi[f][i1];
-      const float tr = br * wr - bi * wi, ti = br * wi + bi * wr;
-      const float ar = zr[f][i0], ai = zi[f][i0];
-      zr[f][i0] = ar + tr;
-      zi[f][i0] = ai + ti;
-      zr[f][i1] = ar - tr;
-      zi[f][i1] = ai - ti;
+  // ---- phase 2: thread (f, k1) -> Z[k1 + 16 k2] = sum_b Y'[b][k1] W16^(b k2)
+  if (tid < kFrames * 16) {
+    const int f = tid >> 4, k1 = tid & 15;
+    float re[16], im[16];
+#pragma unroll
+    for (int bb = 0; bb < 16; ++bb) {
+      re[bb] = yr[f][k1][bb];
+      im[bb] = yi[f][k1][bb];
     }
-    __syncthreads();
+    dft16(re, im, a.cos_tab, a.sin_tab);
+#pragma unroll
+    for (int k2 = 0; k2 < 16; ++k2) {
+      zr[f][k1 + 16 * k2] = re[k2];
+      zi[f][k1 + 16 * k2] = im[k2];
+    }
   }
-  // real-input split -> magnitudes of bins 0..256
-  for (int o = threadIdx.x; o < kFrames * kBins; o += blockDim.x) {
+  __syncthreads();
+  // ---- real-input split -> magnitudes of bins 0..256 (mag reuses yr/yi)
+  for (int o = tid; o < kFrames * kBins; o += blockDim.x) {
     const int f = o / kBins, k = o % kBins;
     const int k1 = k & 255, k2 = (256 - k) & 255;
     const float zkr = zr[f][k1], zki = zi[f][k1];
     const float ckr = zr[f][k2], cki = -zi[f][k2];  // conj Z[256 - k]
     const float er = 0.5f * (zkr + ckr), ei = 0.5f * (zki + cki);
     const float orr = 0.5f * (zki - cki), oi = -0.5f * (zkr - ckr);  // (Z - conj Z') / 2i
-    const float wr = ct[k], wi = -st[k];                              // exp(-2 pi i k / 512)
+    const float wr = __ldg(a.cos_tab + k), wi = -__ldg(a.sin_tab + k);  // exp(-2 pi i k / 512)
     const float xr = er + (orr * wr - oi * wi), xi = ei + (orr * wi + oi * wr);
     mag[f][k] = sqrtf(xr * xr + xi * xi);
   }
   __syncthreads();
   // mel filterbank (sparse row ranges) + log
   float* out = a.mel + static_cast<size_t>(row) * kFrames * kMelBins;
-  for (int o = threadIdx.x; o < kFrames * kMelBins; o += blockDim.x) {
+  for (int o = tid; o < kFrames * kMelBins; o += blockDim.x) {
     const int f = o / kMelBins, m = o % kMelBins;
     const int2 r = a.filter_range[m];
     float acc = 0.0f;
