@@ -400,8 +400,9 @@ int make_op(Ctx& c, GemmOp& op, void* w, const __half* scale, int O, int K, cons
             float post_lo = -INFINITY, float post_hi = INFINITY, __nv_bfloat16* final_bf16 = nullptr) {
   // out_kind: 0 = bf16 tensor, 1 = fp32, 2 = activation that feeds another GEMM
   // (bf16, or fp16 when the weights are int8)
-  op.final_f16 = out_kind == 2 && c.weight_int8;
+  op.final_f16 = out_kind == 2 && c.f16_acts;
   // int8 weights: buckets of >= kWideMinTokens tokens read the fp16 codes
+  // bf16 weights: every bucket reads their exact fp16 copy (same offsets), no scale
   int w_kind = 0;
   if (c.weight_int8) {
     w_kind = 1;
@@ -410,6 +411,10 @@ int make_op(Ctx& c, GemmOp& op, void* w, const __half* scale, int O, int K, cons
       w = static_cast<char*>(c.wide_arena) +
           2 * (static_cast<char*>(w) - static_cast<char*>(c.weight_arena));
     }
+  } else if (c.wide_arena) {
+    w_kind = 2;
+    w = static_cast<char*>(c.wide_arena) + (static_cast<char*>(w) - static_cast<char*>(c.weight_arena));
+    scale = nullptr;
   }
   if (out_kind == 2) out_kind = 0;
   GemmParams& p = op.params;
@@ -746,17 +751,26 @@ int lb_create(const lb_config* cfg, lb_ctx** out_ctx) {
     if (b.rows_cap >= cfg->max_rows) break;
   }
   x->plans.resize(c.buckets.size());
-  cudaStreamCreateWithFlags(&c.capture_stream, cudaStreamNonBlocking);
-  if (cudaStreamCreateWithFlags(&x->copy_stream, cudaStreamNonBlocking) != cudaSuccess) return LB_ERR_CUDA;
+  // from here on a failure hands the partly built context to lb_destroy, which
+  // frees the arenas and whatever streams, events and staging already exist
+  bool ok = cudaStreamCreateWithFlags(&c.capture_stream, cudaStreamNonBlocking) == cudaSuccess &&
+            cudaStreamCreateWithFlags(&x->copy_stream, cudaStreamNonBlocking) == cudaSuccess;
   for (cudaEvent_t* ev : {&x->ev_begin, &x->ev_query, &x->ev_tower, &x->ev_copies})
-    if (cudaEventCreateWithFlags(ev, cudaEventDisableTiming) != cudaSuccess) return LB_ERR_CUDA;
+    ok = ok && cudaEventCreateWithFlags(ev, cudaEventDisableTiming) == cudaSuccess;
+  if (!ok) {
+    lb_destroy(x.release());
+    return LB_ERR_CUDA;
+  }
   x->pinned_bytes = static_cast<size_t>(cfg->max_rows) *
                     (4 + 8 * 3 + 1 + kPcm * 4 + 2 * (cfg->film_query_dim + cfg->output_dims +
                                                       cfg->text_hidden + cfg->film_query_dim) * 2) +
                     4096;
   if (cudaMallocHost(&x->pinned, x->pinned_bytes) != cudaSuccess) x->pinned = nullptr;
   for (auto& kv : c.tensors) x->names.push_back(kv.first);
-  if (cudaDeviceSynchronize() != cudaSuccess) return LB_ERR_CUDA;
+  if (cudaDeviceSynchronize() != cudaSuccess) {
+    lb_destroy(x.release());
+    return LB_ERR_CUDA;
+  }
   *out_ctx = x.release();
   return LB_OK;
 }
@@ -895,6 +909,19 @@ int lb_finalize_weights(lb_ctx* x) {
         c.wide_arena = nullptr;
         return LB_ERR_CUDA;
       }
+    }
+  }
+  if (!c.weight_int8) {
+    // fp16 copy of the bf16 weights (exact for every weight of magnitude >= 2^-14;
+    // the non-GEMM regions of the arena are converted too and never read)
+    const size_t n = c.weight_bytes & ~static_cast<size_t>(15);
+    cudaError_t e = c.wide_arena ? cudaSuccess : cudaMalloc(&c.wide_arena, n);
+    if (e == cudaSuccess) e = widen_bf16_to_f16(c.weight_arena, c.wide_arena, n / 2, nullptr);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(nullptr);
+    if (e != cudaSuccess) {
+      if (c.wide_arena) cudaFree(c.wide_arena);
+      c.wide_arena = nullptr;
+      return LB_ERR_CUDA;
     }
   }
   c.weights_final = true;

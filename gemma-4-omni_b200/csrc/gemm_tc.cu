@@ -332,7 +332,7 @@ __global__ void __launch_bounds__(GemmCfg<TN, WK>::kThreads, 1)
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
       const Unit w = unit_of(u, o_tiles, t_tiles, TN, p.kb_per_split, total_kb);
       const int o = w.o0 + q * 32 + lane;
-      const float scale = SCALED ? __half2float(p.w_scale[o]) : 1.0f;
+      const float scale = SCALED && p.w_scale ? __half2float(p.w_scale[o]) : 1.0f;
       const float bias = (p.bias && w.split == 0) ? p.bias[o] : 0.0f;
       const int b = local & 1;
       if (!mbar_wait(&tmem_full[b], (local >> 1) & 1, p.status)) break;
@@ -509,6 +509,23 @@ __global__ void widen_i8_kernel(const int4* __restrict__ src, int4* __restrict__
   }
 }
 
+// bf16 -> fp16, 8 per thread (saturating: beyond +/-65504 becomes +/-65504).
+__global__ void widen_bf16_kernel(const int4* __restrict__ src, int4* __restrict__ dst, size_t n8) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n8;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const int4 v = src[i];
+    const uint32_t w[4] = {static_cast<uint32_t>(v.x), static_cast<uint32_t>(v.y), static_cast<uint32_t>(v.z),
+                           static_cast<uint32_t>(v.w)};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float lo = __uint_as_float(w[j] << 16), hi = __uint_as_float(w[j] & 0xffff0000u);
+      o[j] = act_bits2(lo, hi, true);
+    }
+    dst[i] = make_int4(static_cast<int>(o[0]), static_cast<int>(o[1]), static_cast<int>(o[2]), static_cast<int>(o[3]));
+  }
+}
+
 int sm_count() {
   int dev = 0, n = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
@@ -591,6 +608,15 @@ cudaError_t widen_int8_codes(const void* src, void* dst, size_t n, cudaStream_t 
   const size_t n16 = n / 16;
   const int blocks = static_cast<int>(n16 / 256 + 1 < 4096 ? n16 / 256 + 1 : 4096);
   widen_i8_kernel<<<blocks, 256, 0, stream>>>(static_cast<const int4*>(src), static_cast<int4*>(dst), n16);
+  return cudaGetLastError();
+}
+
+cudaError_t widen_bf16_to_f16(const void* src, void* dst, size_t n, cudaStream_t stream) {
+  if (n % 8 != 0 || reinterpret_cast<uintptr_t>(src) % 16 || reinterpret_cast<uintptr_t>(dst) % 16)
+    return cudaErrorInvalidValue;
+  const size_t n8 = n / 8;
+  const int blocks = static_cast<int>(n8 / 256 + 1 < 4096 ? n8 / 256 + 1 : 4096);
+  widen_bf16_kernel<<<blocks, 256, 0, stream>>>(static_cast<const int4*>(src), static_cast<int4*>(dst), n8);
   return cudaGetLastError();
 }
 

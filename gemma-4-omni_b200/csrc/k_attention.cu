@@ -390,7 +390,7 @@ cudaError_t launch_attention(Ctx& c, int layer, int rows_cap, cudaStream_t s) {
   a.invalid = c.cfg.invalid_logit;
   a.in_lo = c.w.layers[layer].clip[5][0];
   a.in_hi = c.w.layers[layer].clip[5][1];
-  a.f16 = c.weight_int8 != 0;
+  a.f16 = c.f16_acts != 0;
   const int threads = 32 * c.cfg.heads;
   const size_t smem = attention_smem_bytes(c.cfg.heads, c.hd);
   switch (c.hd) {

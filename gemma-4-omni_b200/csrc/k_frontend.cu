@@ -540,7 +540,7 @@ cudaError_t launch_subsample(Ctx& c, int rows_cap, cudaStream_t s) {
   a.w1 = c.w.conv1;
   a.ln1 = c.w.ln1;
   a.sub_in = c.sub_in;
-  a.f16 = c.weight_int8 != 0;
+  a.f16 = c.f16_acts != 0;
   a.eps = c.cfg.rms_eps;
   a.c1 = c.cfg.sub_ch1;
   int grid = rows_cap < c.num_sms ? rows_cap : c.num_sms;

@@ -456,7 +456,7 @@ cudaError_t launch_row_fused(Ctx& c, int tok_cap, const RowFusedArgs& r, cudaStr
   a.in_hi = r.in_hi;
   a.xa = r.xa;
   a.dbg = r.dbg;
-  a.f16 = c.weight_int8 != 0;
+  a.f16 = c.f16_acts != 0;
   const int grid = tok_cap / 4;  // four tokens (warps) per CTA; tok_cap is a multiple of 32
   switch (c.cfg.hidden / 256) {
     case 1: row_fused_kernel<1><<<grid, 128, 0, s>>>(a); break;
@@ -490,7 +490,7 @@ cudaError_t launch_lconv(Ctx& c, int layer, int rows_cap, cudaStream_t s) {
   a.clip = c.cfg.gradient_clipping;
   a.in_lo = c.w.layers[layer].clip[7][0];  // linear_end input bounds
   a.in_hi = c.w.layers[layer].clip[7][1];
-  a.f16 = c.weight_int8 != 0;
+  a.f16 = c.f16_acts != 0;
   // 256-thread CTAs: 8 sessions of one warp (odd G) or 4 sessions of two warps (even G)
   const int g = c.cfg.hidden / 256;
   const int per_cta = g % 2 == 0 ? 4 : 8;
@@ -525,7 +525,7 @@ cudaError_t launch_outputs(Ctx& c, int tok_cap, int stage, cudaStream_t s) {
   const int width = stage == 0 ? c.cfg.output_dims : c.cfg.text_hidden;
   outputs_kernel<<<tok_cap, width / 8, 0, s>>>(c.dev_counts, c.y, width, stage,
                                                stage == 0 ? c.out_raw : c.out_soft, c.xe,
-                                               c.cfg.rms_eps, c.weight_int8 != 0);
+                                               c.cfg.rms_eps, c.f16_acts != 0);
   return cudaGetLastError();
 }
 
@@ -535,10 +535,10 @@ cudaError_t launch_film(Ctx& c, int tok_cap, int stage, cudaStream_t s) {
     film_norm_kernel<<<tok_cap, 128, 0, s>>>(c.dev_counts, c.in_query, Q, c.out_soft, T,
                                              c.w.fq_norm_w, c.w.fq_norm_b, c.w.fr_norm_w,
                                              c.w.fr_norm_b, c.film_xq, c.film_xr, c.film_amp,
-                                             c.weight_int8 != 0);
+                                             c.f16_acts != 0);
   } else if (stage == 1) {
     film_fuse_kernel<<<tok_cap, 128, 0, s>>>(c.dev_counts, c.film_qd, c.film_gb, B, c.film_fused,
-                                             c.weight_int8 != 0);
+                                             c.f16_acts != 0);
   } else {
     dim3 grid((Q + 255) / 256, tok_cap);
     film_out_kernel<<<grid, 256, 0, s>>>(c.dev_counts, c.film_map, c.in_query, c.film_amp, Q,

@@ -57,6 +57,8 @@ int gemm_prepare(GemmPlan* plan, const void* w, int w_kind, int O, int K, const 
                  int m_cap, void* out, int ld_out, int out_mode, bool out_f16 = false);
 // dst[i] = fp16(src[i]) for n int8 codes (n % 16 == 0, 16-byte aligned).
 cudaError_t widen_int8_codes(const void* src, void* dst, size_t n, cudaStream_t stream);
+// dst[i] = fp16(src[i]) for n bf16 values (n % 8 == 0, 16-byte aligned), saturating.
+cudaError_t widen_bf16_to_f16(const void* src, void* dst, size_t n, cudaStream_t stream);
 cudaError_t gemm_launch(const GemmPlan& plan, GemmParams p, int splits, cudaStream_t stream);
 // K-split count that fills the SMs for an [m_cap x O] output with K reduction.
 int gemm_pick_splits(int O, int K, int m_cap, int num_sms);

@@ -137,6 +137,10 @@ struct Ctx {
   int num_sms = 148;
   int hd = 0;
   int weight_int8 = 0;
+  // GEMM operands are fp16: int8 codes and bf16 weights are both widened to
+  // fp16 exactly, and every activation that feeds a GEMM is stored as fp16
+  // (saturated at +/-65504), 3 more mantissa bits than bf16
+  int f16_acts = 1;
 
   // arenas
   void* weight_arena = nullptr;
