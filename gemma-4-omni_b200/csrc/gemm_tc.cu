@@ -49,9 +49,10 @@ constexpr uint32_t kABytes = kBlockO * kBlockK * 2;  // bf16 A tile, 16 KB
 constexpr uint32_t kRawBytes = kBlockO * kBlockK;    // int8 A tile, 8 KB
 
 // Weight kinds: bf16 weights (bf16 x bf16 MMA); int8 codes widened to fp16
-// in shared memory by converter warps; fp16 codes (int8 codes widened once in
-// HBM), read by TMA like bf16.  Both int8 kinds run fp16 x fp16 MMAs with fp16
-// activations and apply the per-channel scale in the epilogue.
+// in shared memory by converter warps; fp16 weights (int8 codes or bf16 weights
+// widened once in HBM), read by TMA like bf16.  The fp16 kinds run fp16 x fp16
+// MMAs with fp16 activations and apply the per-channel scale, when there is
+// one (int8 codes), in the epilogue.
 constexpr int kWBf16 = 0, kWInt8 = 1, kWF16 = 2;
 
 template <int TN, int WK>
