@@ -75,7 +75,7 @@ def test_gemm_bf16_silu_bias_matches_torch(lib, M, int8):
 @pytest.mark.parametrize("M,splits", [(40, 2), (40, 7), (40, 24), (512, 3), (777, 2)])
 @pytest.mark.parametrize("int8", [0, 1, 2])
 def test_gemm_split_k_atomic_matches_torch(lib, M, splits, int8):
-    # M >= 256 runs on CTA pairs (256-feature tiles), M = 40 on single CTAs
+    # split-K partial sums (fp32 atomics) over one token tile (M = 40) and several (M = 512, 777)
     out, ref = run_gemm(lib, M, 1536, 6144, int8, 2, 0, splits, True, seed=splits + M)
     torch.testing.assert_close(out, ref, rtol=1e-4, atol=1e-4 * ref.abs().max().item())
 
