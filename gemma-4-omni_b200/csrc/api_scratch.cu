@@ -49,11 +49,14 @@ int scratch_setup(int dev, float** out) {
 }
 
 // out[t, o..o+7] = bf16(acc) (act 1: bf16(SiLU(bf16(acc)))), 8 outputs per thread.
+// Writes nothing when the GEMM recorded an error (its sums are then partial).
 __global__ void scratch_finalize_kernel(const float* __restrict__ acc, int m, int width,
-                                        int ld_out, int act, __nv_bfloat16* __restrict__ out) {
+                                        int ld_out, int act, const int* status,
+                                        __nv_bfloat16* __restrict__ out) {
   const int t = blockIdx.y;
   const int o = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
   if (t >= m || o >= width) return;
+  if (status && *status != 0) return;
   const float4* src = reinterpret_cast<const float4*>(acc + static_cast<size_t>(t) * width + o);
   const float4 a = src[0], b = src[1];
   float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
@@ -75,6 +78,10 @@ int lb_op_gemm_splitk_scratch(const void* x, int x_ld, int m, const void* w, int
   if (act < 0 || act > 1 || splits < 1 || ld_out < out_features || ld_out % 8 != 0 ||
       reinterpret_cast<uintptr_t>(out) % 16 != 0)
     return LB_ERR_INVALID_ARGUMENT;
+  // the activation and weight maps start on 16-byte boundaries and rows do not overlap
+  if (x_ld < k || reinterpret_cast<uintptr_t>(x) % 16 != 0 || reinterpret_cast<uintptr_t>(w) % 16 != 0)
+    return LB_ERR_INVALID_ARGUMENT;
+  if (out_features % 128 != 0 || k % 64 != 0) return LB_ERR_INVALID_ARGUMENT;
   const size_t need = static_cast<size_t>(m) * static_cast<size_t>(out_features);
   if (need > kScratchFloats) return LB_ERR_CAPACITY;  // m * out_features > 2^21
   int dev = 0;
@@ -103,7 +110,7 @@ int lb_op_gemm_splitk_scratch(const void* x, int x_ld, int m, const void* w, int
   if (e == cudaSuccess) {
     const int per_block = 128 * 8;
     dim3 grid((out_features + per_block - 1) / per_block, m);
-    scratch_finalize_kernel<<<grid, 128, 0, s>>>(acc, m, out_features, ld_out, act,
+    scratch_finalize_kernel<<<grid, 128, 0, s>>>(acc, m, out_features, ld_out, act, status_dev,
                                                  static_cast<__nv_bfloat16*>(out));
     e = cudaGetLastError();
   }

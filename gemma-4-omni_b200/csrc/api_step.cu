@@ -361,7 +361,7 @@ size_t layout_acts(Ctx& c, char* base) {
   auto sub = a.take<__nv_bfloat16>(T * 32 * 32);
   auto h = a.take<float>(T * d);
   auto y = a.take<float>(T * narrow);
-  auto xa = a.take<__nv_bfloat16>(T * d);
+  auto xa = a.take<__nv_bfloat16>(3 * T * d);  // [3][T][d]: blocks 1, 2 only for split Q/K/V inputs
   auto xf = a.take<__nv_bfloat16>(T * F);
   auto qkv = a.take<__nv_bfloat16>(T * 3 * d);
   auto att = a.take<__nv_bfloat16>(T * d);
@@ -397,7 +397,7 @@ constexpr int kWideMinTokens = 512;
 
 int make_op(Ctx& c, GemmOp& op, void* w, const __half* scale, int O, int K, const void* x, int tok_cap,
             const float* bias, void* out, int out_kind, int act, const float* clip4,
-            float post_lo = -INFINITY, float post_hi = INFINITY, __nv_bfloat16* final_bf16 = nullptr) {
+            float post_lo = -INFINITY, float post_hi = INFINITY, const LayerW* qkv = nullptr) {
   // out_kind: 0 = bf16 tensor, 1 = fp32, 2 = activation that feeds another GEMM
   // (bf16, or fp16 when the weights are int8)
   op.final_f16 = out_kind == 2 && c.f16_acts;
@@ -431,7 +431,22 @@ int make_op(Ctx& c, GemmOp& op, void* w, const __half* scale, int O, int K, cons
   }
   p.post_lo = post_lo;
   p.post_hi = post_hi;
-  const bool finite_out = std::isfinite(p.out_lo) || std::isfinite(p.out_hi);
+  // the fused Q/K/V linear: three stacked parts of O/3 features, each with its
+  // own output clamp and, when their input clamps differ, its own input block
+  int x_parts = 1;
+  bool finite_out = std::isfinite(p.out_lo) || std::isfinite(p.out_hi);
+  if (qkv && (qkv->qkv_split_out || qkv->qkv_split_in)) {
+    p.part_o = O / 3;
+    for (int j = 0; j < 3; ++j) {
+      p.part_lo[j] = qkv->qkv_clip[j][2];
+      p.part_hi[j] = qkv->qkv_clip[j][3];
+      finite_out = finite_out || std::isfinite(p.part_lo[j]) || std::isfinite(p.part_hi[j]);
+    }
+    if (qkv->qkv_split_in) {
+      x_parts = 3;
+      p.x_part_rows = 2 * c.cfg.max_rows;
+    }
+  }
   op.splits = finite_out && out_kind == 1 ? 1 : gemm_pick_splits(O, K, tok_cap, c.num_sms);
   if (out_kind == 0) {
     // A split bf16 output goes through an fp32 partial-sum buffer and a finalize
@@ -447,9 +462,8 @@ int make_op(Ctx& c, GemmOp& op, void* w, const __half* scale, int O, int K, cons
     p.out_mode = out_kind == 0 ? 0 : 1;
     p.out = out;
   }
-  (void)final_bf16;
   return gemm_prepare(&op.plan, w, w_kind, O, K, x, K, tok_cap, p.out, O, p.out_mode,
-                      op.final_f16);
+                      op.final_f16, x_parts, p.x_part_rows);
 }
 
 cudaError_t run_op(Ctx& c, const GemmOp& op, int tok_cap, __nv_bfloat16* final_bf16, cudaStream_t s) {
@@ -462,9 +476,16 @@ cudaError_t run_op(Ctx& c, const GemmOp& op, int tok_cap, __nv_bfloat16* final_b
   if (e != cudaSuccess) return e;
   if (op.splits > 1 && final_bf16) {
     // finalize: output clamp -> activation -> next linear's input clamp -> bf16
-    float clip4[4] = {op.params.out_lo, op.params.out_hi, op.params.post_lo, op.params.post_hi};
+    FinalizeClip fc;
+    fc.part_o = op.params.part_o;
+    for (int j = 0; j < 3; ++j) {
+      fc.lo[j] = fc.part_o ? op.params.part_lo[j] : op.params.out_lo;
+      fc.hi[j] = fc.part_o ? op.params.part_hi[j] : op.params.out_hi;
+    }
+    fc.plo = op.params.post_lo;
+    fc.phi = op.params.post_hi;
     e = launch_finalize_wide(c, tok_cap, static_cast<const float*>(op.params.out), op.plan.O,
-                             op.params.act, final_bf16, clip4, op.final_f16, s);
+                             op.params.act, final_bf16, fc, op.final_f16, s);
   }
   return e;
 }
@@ -490,7 +511,8 @@ int build_plans(lb_ctx* x, int bi) {
       rc |= make_op(c, a1, L.w_ffn1[f], L.s_ffn1[f], F, d, c.xa, tc, nullptr, c.xf, 2, 1, c1, c2[0], c2[1]);
       rc |= make_op(c, a2, L.w_ffn2[f], L.s_ffn2[f], d, F, c.xf, tc, nullptr, c.y, 1, 0, c2);
     }
-    rc |= make_op(c, o.qkv, L.w_qkv, L.s_qkv, 3 * d, d, c.xa, tc, nullptr, c.qkv, 0, 0, L.clip[kLinQkv]);
+    rc |= make_op(c, o.qkv, L.w_qkv, L.s_qkv, 3 * d, d, c.xa, tc, nullptr, c.qkv, 0, 0, L.clip[kLinQkv],
+                  -INFINITY, INFINITY, &L);
     rc |= make_op(c, o.post, L.w_post, L.s_post, d, d, c.att, tc, nullptr, c.y, 1, 0, L.clip[kLinPost]);
     rc |= make_op(c, o.lstart, L.w_lstart, L.s_lstart, 2 * d, d, c.xa, tc, nullptr, c.gl, 0, 0, L.clip[kLinStart]);
     rc |= make_op(c, o.lend, L.w_lend, L.s_lend, d, d, c.xa, tc, nullptr, c.y, 1, 0, L.clip[kLinEnd]);
@@ -558,6 +580,13 @@ cudaError_t run_tower(lb_ctx* x, int bi, int input_kind, cudaStream_t s) {
       r.pre_w = L.norm_pre_attn;
       r.in_lo = L.clip[kLinQkv][0];
       r.in_hi = L.clip[kLinQkv][1];
+      if (L.qkv_split_in) {  // k_proj / v_proj inputs in blocks 1 and 2
+        r.xa_parts = 3;
+        for (int j = 0; j < 2; ++j) {
+          r.part_lo[j] = L.qkv_clip[j + 1][0];
+          r.part_hi[j] = L.qkv_clip[j + 1][1];
+        }
+      }
       r.xa = c.xa;
       LB_TRY(launch_row_fused(c, tc, r, s));
     }
@@ -878,17 +907,33 @@ int lb_finalize_weights(lb_ctx* x) {
       fprintf(stderr, "listener_b200: weight %s was not uploaded\n", kv.first.c_str());
       return LB_ERR_STATE;
     }
+  // Q/K/V bounds: one fused GEMM serves the three projections; where their
+  // bounds differ it clamps per stacked part (outputs) and reads per-part
+  // clamped input blocks (inputs)
   for (int i = 0; i < c.cfg.layers; ++i) {
-    for (int k = 0; k < 4; ++k) {
-      const float b = x->qkv_bounds[i][0][k];
-      if (x->qkv_bounds[i][1][k] != b || x->qkv_bounds[i][2][k] != b) {
-        fprintf(stderr, "listener_b200: q/k/v clip bounds differ in layer %d (unsupported)\n", i);
-        return LB_ERR_INVALID_ARGUMENT;
+    LayerW& L = c.w.layers[i];
+    L.qkv_split_in = L.qkv_split_out = false;
+    for (int q = 0; q < 3; ++q)
+      for (int k = 0; k < 4; ++k) {
+        const float b = x->qkv_bounds[i][q][k];
+        L.qkv_clip[q][k] = b;
+        if (b != x->qkv_bounds[i][0][k]) (k < 2 ? L.qkv_split_in : L.qkv_split_out) = true;
       }
-      c.w.layers[i].clip[kLinQkv][k] = b;
-    }
+    for (int k = 0; k < 4; ++k) L.clip[kLinQkv][k] = x->qkv_bounds[i][0][k];
   }
   cudaSetDevice(c.device);
+  // plans and graphs bake in clip bounds and weight pointers: rebuild them
+  // after every (re)upload
+  if (cudaDeviceSynchronize() != cudaSuccess) return LB_ERR_CUDA;
+  for (auto& pl : x->plans) {
+    for (auto& gph : pl.graph)
+      if (gph) {
+        cudaGraphExecDestroy(gph);
+        gph = nullptr;
+      }
+    pl.built = false;
+    pl.layers.clear();
+  }
   if (!c.rel_bf16_arena &&
       cudaMalloc(&c.rel_bf16_arena, static_cast<size_t>(c.cfg.layers) * 13 * c.cfg.hidden * 2) != cudaSuccess) {
     c.rel_bf16_arena = nullptr;

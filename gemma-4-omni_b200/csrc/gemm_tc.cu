@@ -260,6 +260,8 @@ __global__ void __launch_bounds__(GemmCfg<TN, WK>::kThreads, 1)
       bool ok = true;
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
         const Unit w = unit_of(u, o_tiles, t_tiles, TN, p.kb_per_split, total_kb);
+        // stacked parts (Q/K/V) may read their own activation block
+        const int x_row = w.t0 + (p.x_part_rows ? (w.o0 / p.part_o) * p.x_part_rows : 0);
         for (int i = 0; i < w.nkb; ++i, ++it) {
           const int s = it % S;
           const uint32_t ph = (it / S) & 1;
@@ -274,7 +276,7 @@ __global__ void __launch_bounds__(GemmCfg<TN, WK>::kThreads, 1)
           }
           mbar_arrive_expect_tx(&full[s], tx);
           if (!WINT8) tma_load_2d_nohint(stage_a(s), &tm_w, &full[s], k, w.o0);
-          tma_load_2d(stage_b(s), &tm_x, &full[s], k, w.t0, pol_x);
+          tma_load_2d(stage_b(s), &tm_x, &full[s], k, x_row, pol_x);
         }
       }
     }
@@ -326,12 +328,24 @@ __global__ void __launch_bounds__(GemmCfg<TN, WK>::kThreads, 1)
     const bool f16 = p.out_f16 != 0;
     const bool silu = p.out_mode == 0 && p.act == 1;
     // clamps of the linear output (bf16 / fp32 stores) and of the next input
-    const float lo = p.out_mode == 2 ? -INFINITY : p.out_lo, hi = p.out_mode == 2 ? INFINITY : p.out_hi;
+    // (split-K partial sums are clamped by the finalize pass instead)
+    const bool clip_out = p.out_mode != 2;
+    const bool parts = clip_out && p.part_o > 0;
+    const float lo0 = clip_out ? p.out_lo : -INFINITY, hi0 = clip_out ? p.out_hi : INFINITY;
     const float plo = p.out_mode == 0 ? p.post_lo : -INFINITY, phi = p.out_mode == 0 ? p.post_hi : INFINITY;
-    const bool clamps = isfinite(lo) || isfinite(hi) || isfinite(plo) || isfinite(phi);
+    bool clamps = isfinite(lo0) || isfinite(hi0) || isfinite(plo) || isfinite(phi);
+    if (parts)
+#pragma unroll
+      for (int j = 0; j < GemmParams::kMaxParts; ++j) clamps = clamps || isfinite(p.part_lo[j]) || isfinite(p.part_hi[j]);
     int local = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
       const Unit w = unit_of(u, o_tiles, t_tiles, TN, p.kb_per_split, total_kb);
+      float lo = lo0, hi = hi0;
+      if (parts) {  // selects, not a dynamic index into the parameter block
+        const int j = w.o0 / p.part_o;
+        lo = j == 0 ? p.part_lo[0] : j == 1 ? p.part_lo[1] : p.part_lo[2];
+        hi = j == 0 ? p.part_hi[0] : j == 1 ? p.part_hi[1] : p.part_hi[2];
+      }
       const int o = w.o0 + q * 32 + lane;
       const float scale = SCALED && p.w_scale ? __half2float(p.w_scale[o]) : 1.0f;
       const float bias = (p.bias && w.split == 0) ? p.bias[o] : 0.0f;
@@ -622,9 +636,11 @@ cudaError_t widen_bf16_to_f16(const void* src, void* dst, size_t n, cudaStream_t
 }
 
 int gemm_prepare(GemmPlan* plan, const void* w, int w_kind, int O, int K, const void* x, int x_ld,
-                 int m_cap, void* out, int ld_out, int out_mode, bool out_f16) {
+                 int m_cap, void* out, int ld_out, int out_mode, bool out_f16, int x_parts,
+                 int x_part_rows) {
   if (O % kBlockO != 0 || K % kBlockK != 0 || x_ld % 8 != 0 || ld_out % 8 != 0 || m_cap < 1 ||
-      w_kind < kWBf16 || w_kind > kWF16)
+      w_kind < kWBf16 || w_kind > kWF16 || x_parts < 1 || x_parts > GemmParams::kMaxParts ||
+      (x_parts > 1 && x_part_rows < m_cap))
     return -3;
   const bool w_int8 = w_kind == kWInt8;
   plan->O = O;
@@ -648,9 +664,12 @@ int gemm_prepare(GemmPlan* plan, const void* w, int w_kind, int O, int K, const 
   // tile the box shrinks to m_cap rows; the tile's remaining shared-memory rows
   // then hold stale data that only reaches output columns t >= m_cap, which
   // the epilogue never stores (it stops at the live token count M <= m_cap).
+  // Stacked parts: the map spans every part's block; the rows between a part's
+  // m_cap and the next part's first row feed only columns t >= m_cap as well.
   plan->x_box_rows = m_cap < plan->tn ? m_cap : plan->tn;
+  const uint64_t x_rows = static_cast<uint64_t>(x_parts - 1) * x_part_rows + m_cap;
   // activations are fp16 when the weights are int8 (either kind), bf16 otherwise
-  rc = make_tensor_map_2d(&plan->tm_x, x, 2, K, static_cast<uint64_t>(m_cap),
+  rc = make_tensor_map_2d(&plan->tm_x, x, 2, K, x_rows,
                           static_cast<uint64_t>(x_ld) * 2, kBlockK,
                           static_cast<uint32_t>(plan->x_box_rows), true, w_kind != kWBf16);
   if (rc) return rc;
@@ -667,6 +686,10 @@ cudaError_t gemm_launch(const GemmPlan& plan, GemmParams p, int splits, cudaStre
   p.b_tx_bytes = static_cast<uint32_t>(plan.x_box_rows) * kBlockK * 2;
   p.out_f16 = plan.out_f16 ? 1 : 0;
   if (p.out_mode != plan.out_mode) return cudaErrorInvalidValue;
+  if (p.part_o < 0 || p.x_part_rows < 0 || (p.x_part_rows > 0 && p.part_o == 0) ||
+      (p.part_o > 0 && (p.part_o % kBlockO != 0 || p.O % p.part_o != 0 ||
+                        p.O / p.part_o > GemmParams::kMaxParts)))
+    return cudaErrorInvalidValue;
   const int total_kb = plan.K / kBlockK;
   if (splits < 1) splits = 1;
   if (splits > total_kb) splits = total_kb;

@@ -118,6 +118,11 @@ struct RowFusedDev {
   __nv_bfloat16* xa;
   float* dbg;
   bool f16;  // xa holds fp16 (int8-weight GEMM input) instead of bf16
+  // stacked Q/K/V inputs with their own clamps: blocks 1 and 2 of xa, at
+  // xa_part_stride elements apart, clamped to part_lo/part_hi (0: none)
+  int xa_parts;
+  size_t xa_part_stride;
+  float part_lo[2], part_hi[2];
 };
 
 // One warp per token: lane owns G groups of 8 elements, e = (g*32 + lane)*8,
@@ -207,7 +212,18 @@ __global__ void __launch_bounds__(128, 4) row_fused_kernel(RowFusedDev a) {
         for (int i = 0; i < 8; ++i) w8[i] = 1.0f;
       }
 #pragma unroll
-      for (int i = 0; i < 8; ++i) h[g][i] = fminf(fmaxf(h[g][i] * r * w8[i], a.in_lo), a.in_hi);
+      for (int i = 0; i < 8; ++i) h[g][i] = h[g][i] * r * w8[i];
+      if (a.xa_parts > 1) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          float v[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[i] = fminf(fmaxf(h[g][i], a.part_lo[j]), a.part_hi[j]);
+          store8_act(a.xa + (j + 1) * a.xa_part_stride + base + g * 256, v, a.f16);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) h[g][i] = fminf(fmaxf(h[g][i], a.in_lo), a.in_hi);
       store8_act(a.xa + base + g * 256, h[g], a.f16);
     }
   }
@@ -328,12 +344,16 @@ __global__ void __launch_bounds__(256) lconv_kernel(LconvDev a) {
 
 // ------------------------------------------------------- split-K finalize
 __global__ void finalize_wide_kernel(const int* counts, const float* acc, int width, int act,
-                                     __nv_bfloat16* out, float lo, float hi, float plo, float phi,
-                                     bool f16) {
+                                     __nv_bfloat16* out, FinalizeClip fc, bool f16) {
   const int t = blockIdx.y;
   if (t >= counts[1]) return;
   const int o = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
   if (o >= width) return;
+  // stacked parts: 8 consecutive features never straddle a part (part_o % 128 == 0)
+  const int j = fc.part_o ? o / fc.part_o : 0;
+  const float lo = j == 0 ? fc.lo[0] : j == 1 ? fc.lo[1] : fc.lo[2];
+  const float hi = j == 0 ? fc.hi[0] : j == 1 ? fc.hi[1] : fc.hi[2];
+  const float plo = fc.plo, phi = fc.phi;
   float v[8];
   load8(acc + static_cast<size_t>(t) * width + o, v);
 #pragma unroll
@@ -457,6 +477,13 @@ cudaError_t launch_row_fused(Ctx& c, int tok_cap, const RowFusedArgs& r, cudaStr
   a.xa = r.xa;
   a.dbg = r.dbg;
   a.f16 = c.f16_acts != 0;
+  a.xa_parts = r.xa_parts;
+  a.xa_part_stride = static_cast<size_t>(2) * c.cfg.max_rows * c.cfg.hidden;
+  for (int j = 0; j < 2; ++j) {
+    a.part_lo[j] = r.part_lo[j];
+    a.part_hi[j] = r.part_hi[j];
+  }
+  if (r.xa_parts != 1 && (r.xa_parts != 3 || r.xa != c.xa)) return cudaErrorInvalidValue;
   const int grid = tok_cap / 4;  // four tokens (warps) per CTA; tok_cap is a multiple of 32
   switch (c.cfg.hidden / 256) {
     case 1: row_fused_kernel<1><<<grid, 128, 0, s>>>(a); break;
@@ -509,15 +536,13 @@ cudaError_t launch_lconv(Ctx& c, int layer, int rows_cap, cudaStream_t s) {
 }
 
 cudaError_t launch_finalize_wide(Ctx& c, int tok_cap, const float* acc, int width, int act,
-                                 __nv_bfloat16* out, const float* out_clip, bool out_f16,
+                                 __nv_bfloat16* out, const FinalizeClip& fc, bool out_f16,
                                  cudaStream_t s) {
+  if (fc.part_o < 0 || (fc.part_o && (fc.part_o % 128 || width / fc.part_o > 3)))
+    return cudaErrorInvalidValue;
   const int per_block = 128 * 8;
   dim3 grid((width + per_block - 1) / per_block, tok_cap);
-  finalize_wide_kernel<<<grid, 128, 0, s>>>(c.dev_counts, acc, width, act, out,
-                                            out_clip ? out_clip[0] : -INFINITY,
-                                            out_clip ? out_clip[1] : INFINITY,
-                                            out_clip ? out_clip[2] : -INFINITY,
-                                            out_clip ? out_clip[3] : INFINITY, out_f16);
+  finalize_wide_kernel<<<grid, 128, 0, s>>>(c.dev_counts, acc, width, act, out, fc, out_f16);
   return cudaGetLastError();
 }
 

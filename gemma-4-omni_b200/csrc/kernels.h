@@ -30,6 +30,16 @@ struct GemmParams {
   int* status = nullptr;
   uint32_t b_tx_bytes = 0;  // bytes one activation-tile TMA load delivers (set by gemm_launch)
   int out_f16 = 0;          // out_mode 0 stores fp16 instead of bf16 (set by gemm_launch)
+  // Stacked linears (the fused Q/K/V weight): output features [j*part_o,
+  // (j+1)*part_o) belong to part j (< kMaxParts), which has its own output clamp
+  // part_lo[j]/part_hi[j] (replacing out_lo/out_hi) and reads its activations
+  // x_part_rows * j rows further down X (0: every part reads the same rows).
+  // part_o = 0: one part.  part_o is a multiple of the 128-feature tile.
+  static constexpr int kMaxParts = 3;
+  int part_o = 0;
+  int x_part_rows = 0;
+  float part_lo[kMaxParts] = {-INFINITY, -INFINITY, -INFINITY};
+  float part_hi[kMaxParts] = {INFINITY, INFINITY, INFINITY};
 };
 
 struct GemmPlan {
@@ -52,9 +62,11 @@ int gemm_token_tile(int O, int m_cap, int num_sms);
 // per w_kind) and X ([m_cap,K], row stride x_ld elements; bf16, or fp16 with
 // either int8 kind; TMA zero-fills rows past m_cap).  The output [m_cap, ld_out]
 // is out_mode 0 bf16 (fp16 with out_f16), else fp32; rows past the live token
-// count are never written.
+// count are never written.  x_parts > 1 stacks that many activation blocks,
+// x_part_rows rows apart, in one X map (GemmParams::x_part_rows).
 int gemm_prepare(GemmPlan* plan, const void* w, int w_kind, int O, int K, const void* x, int x_ld,
-                 int m_cap, void* out, int ld_out, int out_mode, bool out_f16 = false);
+                 int m_cap, void* out, int ld_out, int out_mode, bool out_f16 = false,
+                 int x_parts = 1, int x_part_rows = 0);
 // dst[i] = fp16(src[i]) for n int8 codes (n % 16 == 0, 16-byte aligned).
 cudaError_t widen_int8_codes(const void* src, void* dst, size_t n, cudaStream_t stream);
 // dst[i] = fp16(src[i]) for n bf16 values (n % 8 == 0, 16-byte aligned), saturating.

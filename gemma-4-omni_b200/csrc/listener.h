@@ -80,7 +80,10 @@ struct LayerW {
   float* lc_dw;     // [5][d] tap-major (transposed from [d][1][5] on upload)
   void *w_lstart, *w_lend;
   __half *s_lstart, *s_lend;
-  float clip[8][4];  // per linear: in_lo, in_hi, out_lo, out_hi
+  float clip[8][4];  // per linear: in_lo, in_hi, out_lo, out_hi (Q/K/V: the q_proj bounds)
+  float qkv_clip[3][4];  // q_proj, k_proj, v_proj bounds
+  bool qkv_split_in = false;   // their input bounds differ: stacked inputs
+  bool qkv_split_out = false;  // their output bounds differ: per-part output clamps
 };
 
 struct Weights {
@@ -250,6 +253,18 @@ struct RowFusedArgs {
   float in_lo = -INFINITY, in_hi = INFINITY;  // next linear's input clamp
   __nv_bfloat16* xa = nullptr;
   float* dbg = nullptr;           // optional copy of the new h
+  // 3: also write blocks 1 and 2 of the stacked Q/K/V input (xa must be the
+  // context's xa; blocks are 2 * max_rows tokens apart), clamped to
+  // part_lo/part_hi (the K and V input bounds); block 0 gets in_lo/in_hi
+  int xa_parts = 1;
+  float part_lo[2] = {-INFINITY, -INFINITY}, part_hi[2] = {INFINITY, INFINITY};
+};
+// Clamps of the split-K finalize pass: output clamp per stacked part (part_o
+// features each; part_o = 0: one part, lo[0]/hi[0]) and the next input clamp.
+struct FinalizeClip {
+  int part_o = 0;
+  float lo[3] = {-INFINITY, -INFINITY, -INFINITY}, hi[3] = {INFINITY, INFINITY, INFINITY};
+  float plo = -INFINITY, phi = INFINITY;
 };
 cudaError_t launch_row_fused(Ctx& c, int tok_cap, const RowFusedArgs& a, cudaStream_t s);
 cudaError_t launch_attention(Ctx& c, int layer, int rows_cap, cudaStream_t s);
@@ -257,7 +272,7 @@ cudaError_t launch_attention(Ctx& c, int layer, int rows_cap, cudaStream_t s);
 cudaError_t attention_prepare(Ctx& c, cudaStream_t s);
 cudaError_t launch_lconv(Ctx& c, int layer, int rows_cap, cudaStream_t s);
 cudaError_t launch_finalize_wide(Ctx& c, int tok_cap, const float* acc, int width, int act,
-                                 __nv_bfloat16* out, const float* out_clip, bool out_f16, cudaStream_t s);
+                                 __nv_bfloat16* out, const FinalizeClip& clip, bool out_f16, cudaStream_t s);
 cudaError_t launch_outputs(Ctx& c, int tok_cap, int stage, cudaStream_t s);
 cudaError_t launch_film(Ctx& c, int tok_cap, int stage, cudaStream_t s);
 

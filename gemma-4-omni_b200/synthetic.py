@@ -14,6 +14,18 @@ distributions of the reference workload:
 - audio: 16 kHz, 0.05 * N(0,1) white noise plus a 0.1-amplitude sawtooth whose
   pitch glides linearly between two U[150, 300] Hz endpoints over the session.
 - arrivals: start offsets U{0..400} steps, lengths Geometric(1/300) (mean 300).
+
+``nontrivial=True`` (parity runs) perturbs every parameter that the default
+init leaves at an identity value, as a real checkpoint would: norm and
+LayerNorm weights ~ N(1, 0.1), ``per_dim_scale`` ~ N(0, 0.5), the
+``output_proj`` bias and the FiLM LayerNorm biases ~ N(0, 0.05), and finite
+clip bounds on every ``Gemma4ClippableLinear`` (transformers
+models/gemma4/modeling_gemma4.py:128-154): input and output bounds, each
+side drawn separately, so that they bind on a small fraction of the
+elements.  The default-init draws come first and are unchanged, and every
+value of a nontrivial set is then rounded to bf16, as in a bf16 checkpoint
+(the format Gemma 4 weights ship in), so the reference run on them in fp32 is
+the exact target of a bf16-weight step and no weight rounding separates the two.
 """
 from __future__ import annotations
 
@@ -103,14 +115,87 @@ def _draw(rng: np.random.Generator, shape, init: str) -> np.ndarray:
     raise ValueError(init)
 
 
-def synthetic_tower_weights(cfg: ListenerConfig, seed: int = 1234) -> dict[str, np.ndarray]:
-    rng = np.random.default_rng(seed)
-    return {name: _draw(rng, shape, init) for name, shape, init in tower_weight_shapes(cfg)}
+def _bf16_representable(x: float) -> np.ndarray:
+    """0-d float32 array rounded toward zero to 8 significant bits, so the bound
+    is the same in bf16 and fp32 (clip bounds are 0-d buffers in the module)."""
+    v = np.asarray([x], np.float32).view(np.uint32) & np.uint32(0xFFFF0000)
+    return np.asarray(v.view(np.float32)[0], dtype=np.float32)
 
 
-def synthetic_film_weights(cfg: ListenerConfig, seed: int = 4321) -> dict[str, np.ndarray]:
+def clippable_linears(cfg: ListenerConfig) -> list[tuple[str, float]]:
+    """(prefix, typical |input| scale) of every Gemma4ClippableLinear of the tower.
+
+    The scale is the standard deviation the default init gives the linear's
+    input: RMS-normalised rows have unit scale, the FFN's second linear reads
+    SiLU of the first one's output (std 0.02*sqrt(d)), the attention ``post``
+    reads an average of values and ``linear_end`` SiLU of a normalised row.
+    """
+    d = cfg.hidden
+    first = 0.02 * np.sqrt(d)
+    out = []
+    for i in range(cfg.layers):
+        p = f"layers.{i}"
+        for ff in ("feed_forward1", "feed_forward2"):
+            out += [(f"{p}.{ff}.ffw_layer_1", 1.0), (f"{p}.{ff}.ffw_layer_2", 0.5 * first)]
+        out += [(f"{p}.self_attn.{proj}", 1.0) for proj in ("q_proj", "k_proj", "v_proj")]
+        out += [(f"{p}.self_attn.post", first), (f"{p}.lconv1d.linear_start", 1.0),
+                (f"{p}.lconv1d.linear_end", 0.6)]
+    return out
+
+
+def _nontrivial_tower(cfg: ListenerConfig, w: dict[str, np.ndarray], seed: int) -> None:
+    rng = np.random.default_rng([seed, 0x6E6F6E74])
+    for name, shape, init in tower_weight_shapes(cfg):
+        if init == "ones":
+            w[name] = (1.0 + 0.1 * rng.standard_normal(shape)).astype(np.float32)
+        elif name.endswith("per_dim_scale"):
+            w[name] = (0.5 * rng.standard_normal(shape)).astype(np.float32)
+        elif name == "output_proj.bias":
+            w[name] = (0.05 * rng.standard_normal(shape)).astype(np.float32)
+    shapes = {name: shape for name, shape, _ in tower_weight_shapes(cfg)}
+    for prefix, in_scale in clippable_linears(cfg):
+        k_in = shapes[prefix + ".linear.weight"][1]
+        out_scale = 0.02 * np.sqrt(k_in) * in_scale
+        c = rng.uniform(2.0, 3.0, size=4)
+        w[prefix + ".input_min"] = _bf16_representable(-c[0] * in_scale)
+        w[prefix + ".input_max"] = _bf16_representable(c[1] * in_scale)
+        w[prefix + ".output_min"] = _bf16_representable(-c[2] * out_scale)
+        w[prefix + ".output_max"] = _bf16_representable(c[3] * out_scale)
+
+
+def _round_bf16(w: dict[str, np.ndarray]) -> dict[str, np.ndarray]:
+    """Rounds every array to the nearest bf16 value (ties to even), kept as float32."""
+    out = {}
+    for k, v in w.items():
+        shape = np.shape(v)
+        a = np.array(v, dtype=np.float32).reshape(-1)
+        u = a.view(np.uint32).astype(np.uint64)
+        r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16 << 16).astype(np.uint32)
+        out[k] = np.where(np.isfinite(a), r.view(np.float32), a).astype(np.float32).reshape(shape)
+    return out
+
+
+def synthetic_tower_weights(cfg: ListenerConfig, seed: int = 1234, nontrivial: bool = False) -> dict[str, np.ndarray]:
     rng = np.random.default_rng(seed)
-    return {name: _draw(rng, shape, init) for name, shape, init in film_weight_shapes(cfg)}
+    w = {name: _draw(rng, shape, init) for name, shape, init in tower_weight_shapes(cfg)}
+    if nontrivial:
+        _nontrivial_tower(cfg, w, seed)
+        w = _round_bf16(w)
+    return w
+
+
+def synthetic_film_weights(cfg: ListenerConfig, seed: int = 4321, nontrivial: bool = False) -> dict[str, np.ndarray]:
+    rng = np.random.default_rng(seed)
+    w = {name: _draw(rng, shape, init) for name, shape, init in film_weight_shapes(cfg)}
+    if nontrivial:
+        r2 = np.random.default_rng([seed, 0x6E6F6E74])
+        for name, shape, init in film_weight_shapes(cfg):
+            if init == "ones":
+                w[name] = (1.0 + 0.1 * r2.standard_normal(shape)).astype(np.float32)
+            elif init == "zeros":
+                w[name] = (0.05 * r2.standard_normal(shape)).astype(np.float32)
+        w = _round_bf16(w)
+    return w
 
 
 def session_audio(seed: int, session: int, n_frames: int, first_frame: int = 0,

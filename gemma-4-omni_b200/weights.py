@@ -109,7 +109,9 @@ def prepare(cfg: ListenerConfig, tower: dict[str, np.ndarray], film: dict[str, n
                             query_scale(e, cfg.head_dim), _lib.LB_F32))
             continue
         if name.endswith(("input_min", "input_max", "output_min", "output_max")):
-            uploads.append((name, np.asarray([float(w)], np.float32), _lib.LB_F32))
+            # the bf16-rounded bound, like every non-GEMM parameter (a bf16 tower's
+            # clip buffers are bf16); +/-inf stays infinite
+            uploads.append((name, np.asarray(e, np.float32).reshape(1), _lib.LB_F32))
             continue
         uploads.append((name, np.ascontiguousarray(e.reshape(-1)), _lib.LB_F32))
     uploads.append(("frontend.window", hann_window(), _lib.LB_F32))

@@ -208,10 +208,29 @@ int lb_debug_read_buffer(lb_ctx* ctx, const char* name, void* host_dst, size_t b
  * x_ld % 8 == 0); out_mode 0 = bf16, 1 = fp32,
  * 2 = fp32 atomic accumulate (caller zeroes out; required when splits > 1);
  * act 1 = SiLU of the bf16-rounded product (bf16 output only).
- * out_features % 128 == 0, k % 64 == 0. */
+ * out_features % 128 == 0, k % 64 == 0, x_ld >= k, ld_out >= out_features,
+ * x and w 16-byte aligned (else LB_ERR_INVALID_ARGUMENT). */
 int lb_op_gemm(const void* x, int x_ld, int m, const void* w, int w_int8, const void* w_scale,
                const float* bias, int out_features, int k, void* out, int ld_out, int out_mode,
                int act, int splits, int* status_dev, void* stream);
+
+/* lb_op_gemm with the clip bounds of Gemma4ClippableLinear
+ * (transformers models/gemma4/modeling_gemma4.py:128-154, whose output clamp
+ * the reference's Triton linear fuses, streaming_conformer_kernels.py:27-73).
+ * The weight is `parts` stacked linears of out_features/parts features each
+ * (3: the fused q/k/v projections; out_features % (128*parts) == 0):
+ * out_bounds[2j], out_bounds[2j+1] clamp part j's linear output before the
+ * activation; post_bounds[0..1] clamp after it (the next linear's input
+ * clamp; bf16 output only).  A null array means +/-inf.  x_part_rows > 0
+ * (parts > 1, >= m): part j reads its activations from x rows
+ * [j*x_part_rows, j*x_part_rows + m) (per-part input clamps applied by the
+ * producer of x); 0: every part reads rows [0, m).  Finite bounds need
+ * out_mode 0 or 1 (split-K partial sums are not clamped). */
+int lb_op_gemm_clipped(const void* x, int x_ld, int m, int x_part_rows, const void* w, int w_int8,
+                       const void* w_scale, const float* bias, int out_features, int k, void* out,
+                       int ld_out, int out_mode, int act, int splits, int parts,
+                       const float* out_bounds, const float* post_bounds, int* status_dev,
+                       void* stream);
 
 /* ----------------------------------------------------------------------
  * Tick-level row selection (device arrays, asynchronous on `stream`).
@@ -257,6 +276,8 @@ int lb_order_ready_heads(int n_heads, const int64_t* ready_at_ns, const int64_t*
  * current) resolves the array's address and sets the GEMM kernel attributes,
  * so make it before any stream capture.  There is one array per device:
  * calls that overlap on the GPU race.  x / w / w_scale / bias as lb_op_gemm.
+ * `out` is undefined whenever *status_dev != 0 after the call (the GEMM gave
+ * up on a bounded wait): the rounding pass then leaves it unwritten.
  * No counterpart in the reference: it exists for callers that must not
  * allocate device memory per call. */
 int lb_op_gemm_splitk_scratch(const void* x, int x_ld, int m, const void* w, int w_int8,

@@ -18,10 +18,19 @@ Fixtures:
                      epoch change and input masks
   tower_small.npz    same at the SMALL config (d=256) used by the GPU parity tests
   tower_full.npz     the BASELINE config-0 tower (d=1536, 12 layers), 1 session x 4 ticks
-  film.npz           FrameResidualQueryFiLMAdapter (1536/2048/256 and the SMALL dims)
+  tower_small_nt.npz the SMALL trace with non-identity parameters (synthetic
+                     ``nontrivial=True``: norm weights, per_dim_scale, output_proj
+                     bias and finite clip bounds on every clippable linear)
+  tower_full_nt.npz  the config-0 tower with non-identity parameters over the
+                     first 18 ticks of the 3-session trace (reorder, cursor gap,
+                     epoch change, input masks)
+  film.npz           FrameResidualQueryFiLMAdapter (1536/2048/256 and the SMALL dims),
+                     default and non-identity LayerNorm parameters
   packer.npz         slot ids / reasons / committed positions of the tower's slot
-                     policy, the tick dispatcher's snapshot order, and the
-                     coordinator's head order on seeded event traces
+                     policy (``events``), the tick dispatcher's snapshot order
+                     (``dispatch``), and the ListenerMicrobatchCoordinator's
+                     dispatched rows and reasons on a seeded enqueue/take trace
+                     (``coordinator``)
 """
 from __future__ import annotations
 
@@ -103,6 +112,8 @@ def tower_trace(cfg, seed: int, kind: str):
         plan.append([("A", 1, "e1", k - 6), ("B", 0, "e0", k - 1), ("C", 0, "e0", k - 7)])
     if kind == "full":
         plan = [[("A", 0, "e0", i)] for i in range(4)]
+    if kind == "full_nt":
+        plan = plan[:18]
     for t, rows in enumerate(plan):
         mel = rng.standard_normal((len(rows), 8, 128), dtype=np.float32)
         mask = np.ones((len(rows), 8), dtype=bool)
@@ -112,14 +123,14 @@ def tower_trace(cfg, seed: int, kind: str):
     return ticks
 
 
-def run_tower(pkg, cfg, seed_w: int, seed_trace: int, kind: str):
+def run_tower(pkg, cfg, seed_w: int, seed_trace: int, kind: str, nontrivial: bool = False):
     from duplex_kernel.streaming_conformer import AudioStreamCursor, StreamingConformerAudioTower
     from gemma4_omni_b200.synthetic import synthetic_tower_weights
 
-    tower_w = synthetic_tower_weights(cfg, seed_w)
+    tower_w = synthetic_tower_weights(cfg, seed_w, nontrivial=nontrivial)
     tower, embed = build_reference_tower(cfg, tower_w)
     st = StreamingConformerAudioTower(tower, embed, device="cpu", dtype=torch.float32, max_sessions=6)
-    out = {"seed_w": seed_w, "seed_trace": seed_trace}
+    out = {"seed_w": seed_w, "seed_trace": seed_trace, "nontrivial": np.bool_(nontrivial)}
     rows_meta, raws, softs, subs, layers, slots, reasons = [], [], [], [], [], [], []
     mels, masks = [], []
     with torch.inference_mode():
@@ -170,8 +181,9 @@ def make_film(pkg):
     from gemma4_omni_b200.synthetic import synthetic_film_weights
 
     out = {}
-    for tag, cfg in (("full", FULL), ("small", SMALL)):
-        w = synthetic_film_weights(cfg, 77)
+    for tag, cfg, nt in (("full", FULL, False), ("small", SMALL, False), ("full_nt", FULL, True),
+                         ("small_nt", SMALL, True)):
+        w = synthetic_film_weights(cfg, 77, nontrivial=nt)
         w["output.weight"] = w["output.weight"] * 300.0  # make the residual clearly non-trivial
         ad = FrameResidualQueryFiLMAdapter(cfg.text_hidden, cfg.film_query_dim, cfg.film_bottleneck).eval()
         ad.load_state_dict({k: torch.from_numpy(np.asarray(v)) for k, v in w.items()}, strict=True)
@@ -265,26 +277,113 @@ def make_packer(pkg):
     dispatch = {"frames": frames_in, "paused": ["d3"], "registrations": ["d0", "d1", "d2", "d3", "d4"],
                 "tick0": tick0, "deferred0": deferred0, "tick1": tick1, "deadline0": deadline,
                 "deadline1": 3_000_000}
-    return {"events": json.dumps(events), "max_sessions": np.int64(S), "dispatch": json.dumps(dispatch)}
+    return {"events": json.dumps(events), "max_sessions": np.int64(S), "dispatch": json.dumps(dispatch),
+            "coordinator": json.dumps(make_coordinator())}
+
+
+def make_coordinator():
+    """ListenerMicrobatchCoordinator.take_ready on a seeded enqueue/take trace.
+
+    Sessions are registered in a shuffled order; frames arrive with jittered
+    ready times (ties included, so submission order and session id break
+    them); take_ready runs at times that hit the 2 ms singleton coalesce window
+    on both sides; a batch stays in flight for a random number of takes (no
+    further batch while one is active) before ``complete``.  Records every
+    take's dispatched (session, frame) rows in order and its reason.
+    """
+    from duplex_kernel.listener_microbatch import ListenerMicrobatchCoordinator
+    from duplex_kernel.microbatch_contract import (ListenerFrame, ListenerSessionState, NativeBatchCapability,
+                                                   RowStateUpdate, RuntimeSignature)
+
+    sig = RuntimeSignature(model_id="google/gemma-4-E2B-it", model_config_sha256="a" * 64,
+                           checkpoint_sha256="b" * 64, topology_sha256="c" * 64,
+                           native_library_sha256="d" * 64, native_abi_version=3, batch_api_version=2,
+                           attention_backend_id=3, rmsnorm_backend_id=2, max_seq_len=16_384, stream_q_len=2)
+    cap = NativeBatchCapability(api_version=2, native_abi_version=3, attention_backend_id=3,
+                                rmsnorm_backend_id=2, max_seq_len=16_384, stream_q_len=2,
+                                supports_arbitrary_batch_size=True, stream_priority=-1,
+                                stream_identity="listener-stream")
+    coord = ListenerMicrobatchCoordinator(sig, cap)
+    rng = np.random.default_rng(4242)
+    sessions = [f"c{i:02d}" for i in rng.permutation(6)]
+    for i, sid in enumerate(sessions):
+        coord.register_session(ListenerSessionState(
+            session_id=sid, generation_id=1, state_epoch_id=f"ep-{sid}", runtime_signature=sig,
+            next_frame_id=0, state_version=0, sequence_position=0, cache_position=34,
+            valid_history_tokens=34, native_context_id=20_000 + i))
+    next_frame = {sid: 0 for sid in sessions}
+    events = []
+    now = 1_000_000
+    active = None
+    hold = 0
+    for step in range(160):
+        now += int(rng.choice([0, 300_000, 1_000_000, 1_999_999, 2_000_000, 2_500_000, 80_000_000]))
+        for _ in range(int(rng.choice([0, 0, 1, 1, 1, 2, 4, 6]))):
+            sid = sessions[int(rng.integers(0, len(sessions)))]
+            ready = now + int(rng.choice([-3_000_000, -2_000_000, -500_000, 0, 0, 700_000, 4_000_000]))
+            ready = max(ready, 0)
+            coord.enqueue(ListenerFrame(session_id=sid, generation_id=1, state_epoch_id=f"ep-{sid}",
+                                        frame_id=next_frame[sid], ready_at_ns=ready,
+                                        pcm=np.zeros(1280, np.float32)))
+            events.append({"kind": "enqueue", "sid": sid, "frame": next_frame[sid], "ready_at": ready})
+            next_frame[sid] += 1
+        if active is not None:
+            if hold > 0:
+                hold -= 1
+                events.append({"kind": "take", "now": now, "rows": None, "reason": None, "active": True})
+                assert coord.take_ready(now) is None
+                continue
+            coord.complete(active, tuple(RowStateUpdate(session_id=r.session_id, frame_id=r.frame_id,
+                                                        cache_position=r.cache_position + 2,
+                                                        valid_history_tokens=r.cache_position + 2)
+                                         for r in active.manifest.rows))
+            events.append({"kind": "complete"})
+            active = None
+        batch = coord.take_ready(now)
+        if batch is None:
+            events.append({"kind": "take", "now": now, "rows": None, "reason": None, "active": False})
+            continue
+        rows = [[r.session_id, r.frame_id] for r in batch.manifest.rows]
+        events.append({"kind": "take", "now": now, "rows": rows, "reason": batch.manifest.dispatch_reason,
+                       "active": False})
+        active = batch
+        hold = int(rng.integers(0, 3))
+    return {"registrations": sessions, "coalesce_ns": coord.coalesce_window_ns, "events": events}
 
 
 def main() -> None:
+    """``make_golden.py <reference checkout> [fixture ...]``: writes every
+    fixture, or only the named ones (file stems, e.g. ``tower_full_nt``)."""
     ref = Path(sys.argv[1] if len(sys.argv) > 1 else "/nonexistent")
     if str(ref) not in sys.path:
         sys.path.insert(0, str(ref))
+    only = set(sys.argv[2:])
     torch.set_num_threads(4)
     pkg = load_pkg()
     from gemma4_omni_b200.config import FULL, SMALL
 
-    np.savez_compressed(HERE / "mel.npz", **make_mel(pkg))
-    np.savez_compressed(HERE / "film.npz", **make_film(pkg))
-    np.savez_compressed(HERE / "packer.npz", **make_packer(pkg))
-    np.savez_compressed(HERE / "tower_tiny.npz", **run_tower(pkg, tiny_config(pkg), 23, 9917, "tiny"))
-    np.savez_compressed(HERE / "tower_small.npz", **run_tower(pkg, SMALL, 31, 712, "small"))
-    full = run_tower(pkg, FULL, 41, 125, "full")
-    full.pop("layers")  # keep the fixture small: raw/soft/sub only
-    np.savez_compressed(HERE / "tower_full.npz", **full)
-    print("golden fixtures written to", HERE)
+    def full_tower(seed_w, seed_trace, kind, nontrivial=False):
+        out = run_tower(pkg, FULL, seed_w, seed_trace, kind, nontrivial=nontrivial)
+        out.pop("layers")  # keep the fixture small: raw/soft/sub only
+        return out
+
+    makers = {
+        "mel": lambda: make_mel(pkg),
+        "film": lambda: make_film(pkg),
+        "packer": lambda: make_packer(pkg),
+        "tower_tiny": lambda: run_tower(pkg, tiny_config(pkg), 23, 9917, "tiny"),
+        "tower_small": lambda: run_tower(pkg, SMALL, 31, 712, "small"),
+        "tower_full": lambda: full_tower(41, 125, "full"),
+        "tower_small_nt": lambda: run_tower(pkg, SMALL, 33, 713, "small", nontrivial=True),
+        "tower_full_nt": lambda: full_tower(43, 126, "full_nt", nontrivial=True),
+    }
+    unknown = only - set(makers)
+    if unknown:
+        raise SystemExit(f"unknown fixtures: {sorted(unknown)}")
+    for name, make in makers.items():
+        if not only or name in only:
+            np.savez_compressed(HERE / f"{name}.npz", **make())
+            print("wrote", HERE / f"{name}.npz")
 
 
 if __name__ == "__main__":

@@ -77,3 +77,72 @@ def mask_bits(mask: np.ndarray) -> torch.Tensor:
 
 def golden_rows(g):
     return json.loads(str(g["rows"])), json.loads(str(g["reasons"]))
+
+
+def replay_coordinator(golden: dict, order_fn) -> int:
+    """Replays the reference ListenerMicrobatchCoordinator golden trace
+    (listener_microbatch.py:144-279) through ``order_fn(heads, now_ns,
+    coalesce_ns, registered) -> (rows, reason)``: per-session FIFO queues with a
+    global submission counter, the head of every queue as a candidate, no take
+    while a batch is in flight.  Asserts every take's rows and reason; returns
+    the number of takes checked."""
+    from collections import deque
+
+    queues = {sid: deque() for sid in golden["registrations"]}
+    order = 0
+    in_flight = False
+    checked = 0
+    for ev in golden["events"]:
+        if ev["kind"] == "enqueue":
+            queues[ev["sid"]].append((ev["ready_at"], order, ev["sid"], ev["frame"]))
+            order += 1
+        elif ev["kind"] == "complete":
+            assert in_flight
+            in_flight = False
+        else:
+            if ev["active"]:
+                assert in_flight and ev["rows"] is None
+                continue
+            assert not in_flight
+            heads = [q[0][:3] for q in queues.values() if q]
+            rows, reason = order_fn(heads, ev["now"], golden["coalesce_ns"], len(golden["registrations"]))
+            if ev["rows"] is None:
+                assert (rows, reason) == ([], None), (ev, rows, reason)
+            else:
+                got = []
+                for h in rows:
+                    ready_at, sub, sid, frame = queues[h[2]].popleft()
+                    assert (ready_at, sub) == (h[0], h[1])
+                    got.append([sid, frame])
+                assert got == ev["rows"] and reason == ev["reason"], (ev, got, reason)
+                in_flight = True
+            checked += 1
+    return checked
+
+
+def replay_oracle_trace(model, g):
+    """Drives the CPU oracle through a golden tower trace (rows, reasons, slots,
+    mel, mask); returns (raw, soft, sub, layers) stacked like the golden."""
+    rows = json.loads(str(g["rows"]))
+    reasons = json.loads(str(g["reasons"]))
+    slots = g["slots"]
+    state: dict[int, dict] = {}
+    zero = {k: v[0] for k, v in conformer_ref.zero_state(model.cfg, 1).items()}
+    raws, softs, subs, layers = [], [], [], []
+    off = 0
+    for tick_rows, tick_reasons in zip(rows, reasons):
+        n = len(tick_rows)
+        sl = [int(s) for s in slots[off:off + n]]
+        st = {k: torch.stack([state.get(s, zero)[k] for s in sl]) for k in zero}
+        reset = torch.tensor([r != "continue" for r in tick_reasons])
+        mel = torch.from_numpy(g["mel"][off:off + n])
+        mask = torch.from_numpy(g["mask"][off:off + n])
+        raw, soft, sub, lay, nxt = model.step(mel, mask, st, reset)
+        for i, s in enumerate(sl):
+            state[s] = {k: v[i] for k, v in nxt.items()}
+        raws.append(raw)
+        softs.append(soft)
+        subs.append(sub)
+        layers.append(torch.stack(lay))
+        off += n
+    return torch.cat(raws), torch.cat(softs), torch.cat(subs), torch.cat(layers, dim=1)

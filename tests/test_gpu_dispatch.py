@@ -100,3 +100,17 @@ def test_order_rejects_more_than_capacity(dispatch):
     heads = [(0, i, f"s{i}") for i in range(dispatch.MAX_SORT_HEADS + 1)]
     with pytest.raises(RuntimeError):
         dispatch.order_ready_heads(heads, 0, 0, len(heads))
+
+
+def test_order_replays_reference_coordinator_golden(dispatch):
+    """lb_order_ready_heads through the reference ListenerMicrobatchCoordinator's
+    take_ready trace (tests/golden/packer.npz ``coordinator``): every dispatched
+    row order and reason bit-exact."""
+    import json
+    from pathlib import Path
+
+    import numpy as np
+    from helpers import replay_coordinator
+
+    g = json.loads(str(np.load(Path(__file__).resolve().parent / "golden" / "packer.npz")["coordinator"]))
+    assert replay_coordinator(g, dispatch.order_ready_heads) > 50

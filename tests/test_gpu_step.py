@@ -1,8 +1,16 @@
 """Listener step on the GPU vs the reference goldens and the CPU oracle.
 
-Tolerance (bf16 weights/activations vs the fp32 reference): per-frame cosine
->= 0.999 and max|a-b|/max|b| <= 2e-2 (tests/helpers.py).  Packing (slot ids,
-reasons) is compared bit-exactly.
+Tolerance: per-frame cosine >= 0.999 and max|a-b|/max|b| <= 2e-2
+(tests/helpers.py), for both weight formats.  bf16 weights are checked
+against the fp32 reference itself; int8 weights against the fp32 oracle run
+on the same dequantised weights (kernel error only), and separately against
+the unquantised reference golden with a looser bound that includes the
+quantisation error.  Packing (slot ids, reasons) is compared bit-exactly.
+
+Most cases use the non-identity parameter set (synthetic ``nontrivial``):
+norm weights, per_dim_scale, output_proj bias, FiLM LayerNorm parameters and
+finite clip bounds on every clippable linear all take non-trivial values, so
+a kernel that ignored or mis-indexed any of them fails.
 """
 from __future__ import annotations
 
@@ -13,7 +21,7 @@ import pytest
 import torch
 
 from helpers import (HandleBook, assert_parity, film_weights_from_engine, golden_rows, mask_bits,
-                     oracle_from_engine)
+                     oracle_from_engine, replay_oracle_trace)
 from oracle import conformer_ref, film_ref, mel_ref
 
 pytestmark = pytest.mark.gpu
@@ -21,15 +29,44 @@ GOLD = Path(__file__).resolve().parent / "golden"
 REASON_CODES = {"continue": 0, "reset": 1, "gap_or_cursor_mismatch": 2, "identity_reset": 3}
 
 
-def make_engine(cfg, fmt=0, sessions=8, rows=None, tower_seed=11, film_seed=12, film_scale=1.0, handles=None):
+# int8 vs the unquantised reference: quantisation error on top of kernel error.
+# The fp32 oracle on the dequantised weights alone (no kernel error) sits at
+# cosine 0.9981 / rel 6.8e-2 from the FULL non-identity golden (18 ticks) and
+# 0.9998 / 2.5e-2 from the SMALL one.
+INT8_VS_GOLDEN = (0.995, 1e-1)
+
+
+def make_engine(cfg, fmt=0, sessions=8, rows=None, tower_seed=11, film_seed=12, film_scale=1.0, handles=None,
+                nontrivial=False):
     from gemma4_omni_b200 import runtime, synthetic
 
     eng = runtime.ListenerEngine(cfg, max_sessions=sessions, max_rows=rows, max_handles=handles,
                                  weight_format=fmt)
-    fw = synthetic.synthetic_film_weights(cfg, film_seed)
+    fw = synthetic.synthetic_film_weights(cfg, film_seed, nontrivial=nontrivial)
     fw["output.weight"] = fw["output.weight"] * film_scale
-    eng.load_weights(synthetic.synthetic_tower_weights(cfg, tower_seed), fw)
+    eng.load_weights(synthetic.synthetic_tower_weights(cfg, tower_seed, nontrivial=nontrivial), fw)
     return eng
+
+
+def is_nontrivial(g) -> bool:
+    return bool(g["nontrivial"]) if "nontrivial" in g.files else False
+
+
+def check_replay(eng, g, out, layers=True):
+    """bf16: the gate against the reference golden.  int8: the gate against the
+    oracle on the dequantised weights, and INT8_VS_GOLDEN against the golden."""
+    keys = ["sub", "layers", "raw", "soft"] if layers else ["sub", "raw", "soft"]
+    names = {"sub": "subsampled", "layers": "layers", "raw": "raw", "soft": "soft"}
+    gold = {k: torch.from_numpy(g[k]) for k in keys}
+    if eng.weight_format == 0:
+        for k in keys:
+            assert_parity(out[k], gold[k], names[k])
+        return
+    raw, soft, sub, lay = replay_oracle_trace(oracle_from_engine(eng), g)
+    ref = {"sub": sub, "layers": lay, "raw": raw, "soft": soft}
+    for k in keys:
+        assert_parity(out[k], ref[k], names[k] + " vs oracle")
+        assert_parity(out[k], gold[k], names[k] + " vs golden", *INT8_VS_GOLDEN)
 
 
 def replay_golden(eng, g, debug=True):
@@ -57,32 +94,29 @@ def replay_golden(eng, g, debug=True):
     return {k: torch.cat(v, dim=1 if k == "layers" else 0) for k, v in outs.items() if v}
 
 
+@pytest.mark.parametrize("fixture", ["tower_small", "tower_small_nt"])
 @pytest.mark.parametrize("fmt", [0, 1])
-def test_small_tower_replays_reference_trace(pkg, fmt):
+def test_small_tower_replays_reference_trace(pkg, fixture, fmt):
     """Reorder, reset, cursor gap, epoch change and input masks (reference trace)."""
     from gemma4_omni_b200.config import SMALL
 
-    g = np.load(GOLD / "tower_small.npz")
-    eng = make_engine(SMALL, fmt, sessions=6, tower_seed=int(g["seed_w"]))
+    g = np.load(GOLD / f"{fixture}.npz")
+    eng = make_engine(SMALL, fmt, sessions=6, tower_seed=int(g["seed_w"]), nontrivial=is_nontrivial(g))
     out = replay_golden(eng, g)
-    # the golden is the fp32 reference; int8 adds quantisation error on top of bf16
-    cos_min = 0.999 if fmt == 0 else 0.995
-    assert_parity(out["sub"], torch.from_numpy(g["sub"]), "subsampled", cos_min)
-    assert_parity(out["layers"], torch.from_numpy(g["layers"]), "layers", cos_min, 4e-2 if fmt else 2e-2)
-    assert_parity(out["raw"], torch.from_numpy(g["raw"]), "raw", cos_min, 4e-2 if fmt else 2e-2)
-    assert_parity(out["soft"], torch.from_numpy(g["soft"]), "soft", cos_min, 4e-2 if fmt else 2e-2)
+    check_replay(eng, g, out)
     eng.close()
 
 
-def test_full_tower_matches_reference_golden(pkg):
+@pytest.mark.parametrize("fixture,fmt", [("tower_full", 0), ("tower_full_nt", 0), ("tower_full_nt", 1)])
+def test_full_tower_matches_reference_golden(pkg, fixture, fmt):
+    """BASELINE config-0 tower (d=1536, 12 layers); the _nt trace has 3 sessions
+    over 18 ticks with reorder, cursor gap, epoch change and masks."""
     from gemma4_omni_b200.config import FULL
 
-    g = np.load(GOLD / "tower_full.npz")
-    eng = make_engine(FULL, 0, sessions=4, tower_seed=int(g["seed_w"]))
-    out = replay_golden(eng, g)
-    assert_parity(out["sub"], torch.from_numpy(g["sub"]), "subsampled")
-    assert_parity(out["raw"], torch.from_numpy(g["raw"]), "raw")
-    assert_parity(out["soft"], torch.from_numpy(g["soft"]), "soft")
+    g = np.load(GOLD / f"{fixture}.npz")
+    eng = make_engine(FULL, fmt, sessions=4, tower_seed=int(g["seed_w"]), nontrivial=is_nontrivial(g))
+    out = replay_golden(eng, g, debug=True)
+    check_replay(eng, g, out, layers=False)
     eng.close()
 
 
@@ -113,14 +147,15 @@ def test_mel_kernel_matches_reference_extractor(pkg):
     eng.close()
 
 
-@pytest.mark.parametrize("fmt,steps,n", [(0, 500, 2), (1, 200, 2)])
+@pytest.mark.parametrize("fmt,steps,n", [(0, 500, 1), (0, 500, 2), (0, 500, 4), (1, 500, 4)])
 def test_full_config_carried_parity_over_many_steps(pkg, fmt, steps, n):
-    """PCM -> soft tokens, state carried across `steps` ticks, vs the CPU oracle."""
+    """N time-aligned sessions, PCM -> soft tokens, state
+    carried across 500 ticks, vs the CPU oracle at the gate (both formats)."""
     from gemma4_omni_b200 import _lib, synthetic
     from gemma4_omni_b200.config import FULL
 
     torch.set_num_threads(max(1, torch.get_num_threads()))
-    eng = make_engine(FULL, fmt, sessions=4)
+    eng = make_engine(FULL, fmt, sessions=4, nontrivial=True)
     model = oracle_from_engine(eng)
     state = conformer_ref.zero_state(model.cfg, n)
     pcm_all = np.stack([synthetic.session_audio(21, s, steps, total_frames=steps) for s in range(n)], axis=1)
@@ -141,8 +176,7 @@ def test_full_config_carried_parity_over_many_steps(pkg, fmt, steps, n):
         reset = torch.full((n,), t == 0)
         _, soft, _, _, state = model.step(torch.from_numpy(np.stack(mels)), torch.ones(n, 8, dtype=torch.bool),
                                           state, reset)
-        c, r = assert_parity(out["soft"], soft, f"soft step {t}", 0.999 if fmt == 0 else 0.998,
-                             2e-2 if fmt == 0 else 3e-2)
+        c, r = assert_parity(out["soft"], soft, f"soft step {t}")
         worst_cos, worst_rel = min(worst_cos, c), max(worst_rel, r)
     assert eng.status() == 0
     print(f"fmt={fmt} steps={steps}: worst cosine {worst_cos:.6f}, worst rel {worst_rel:.3e}")
@@ -155,7 +189,7 @@ def test_ragged_continuous_batching_matches_oracle(pkg):
     from gemma4_omni_b200.config import SMALL
 
     rng = np.random.default_rng(5)
-    eng = make_engine(SMALL, 0, sessions=24, rows=24, film_scale=300.0, handles=64)
+    eng = make_engine(SMALL, 0, sessions=24, rows=24, film_scale=300.0, handles=64, nontrivial=True)
     model = oracle_from_engine(eng)
     fw = film_weights_from_engine(eng)
     arrivals = synthetic.ArrivalProcess(40, seed=3, mean_len=12, start_max=20, mode="pool")
@@ -198,6 +232,68 @@ def test_ragged_continuous_batching_matches_oracle(pkg):
         ref_film = film_ref.film_forward(fw, out["soft"].float().cpu(), query.float())
         assert_parity(out["film"], ref_film, f"film step {t}", 0.9999, 1e-2)
     assert eng.status() == 0
+    eng.close()
+
+
+def test_config2_full_tower_256_ragged_sessions_matches_oracle(pkg):
+    """BASELINE config 2 at its stated size: 256 sessions on the FULL bf16 tower
+    (+ FiLM), geometric lengths (mean 300), start offsets spread so that the
+    packed batch grows from a few rows to ~200 over the run; sessions join every
+    step, some leave, rows arrive shuffled, cache positions differ per session.
+    Start offsets are drawn from U{0..32} instead of U{0..400} so that 36 steps
+    cover the 1..256-row range the config describes."""
+    from gemma4_omni_b200 import _lib, synthetic
+    from gemma4_omni_b200.config import FULL
+
+    torch.set_num_threads(max(1, torch.get_num_threads()))
+    rng = np.random.default_rng(15)
+    S = 256
+    eng = make_engine(FULL, 0, sessions=S, rows=S, handles=2 * S, nontrivial=True, film_scale=300.0)
+    model = oracle_from_engine(eng)
+    fw = film_weights_from_engine(eng)
+    arrivals = synthetic.ArrivalProcess(S, seed=21, mean_len=300, start_max=32, mode="pool")
+    states: dict[int, dict] = {}
+    zero = {k: v[0] for k, v in conformer_ref.zero_state(model.cfg, 1).items()}
+    tails: dict[int, np.ndarray | None] = {}
+    sizes = []
+    for t in range(36):
+        lanes, sids, frames, _ = arrivals.step()
+        live = set(int(x) for x in sids)
+        for sid in list(states):
+            if sid not in live:  # the session ended: release its slot
+                eng.reset_handle(sid)
+                states.pop(sid)
+        if len(sids) == 0:
+            continue
+        order = rng.permutation(len(sids))
+        sids, frames = sids[order], frames[order]
+        n = len(sids)
+        sizes.append(n)
+        h = torch.from_numpy(sids.astype(np.int32)).cuda()
+        z = torch.zeros(n, dtype=torch.int64, device="cuda")
+        fr = torch.from_numpy(frames.astype(np.int64)).cuda()
+        eng.pack(h, z, fr, fr.clone())
+        pcm = np.stack([synthetic.session_audio(17, int(x), 1, first_frame=int(f), total_frames=300)[0]
+                        for x, f in zip(sids, frames)])
+        query = torch.randn(n, 2, FULL.film_query_dim, generator=torch.Generator().manual_seed(t)).to(torch.bfloat16)
+        out = eng.step(torch.from_numpy(pcm).cuda(), kind=_lib.LB_INPUT_PCM, query=query.cuda())
+        eng.commit()
+        mels = []
+        for i, x in enumerate(sids):
+            m, tails[int(x)] = mel_ref.extract_single_frame(pcm[i], tails.get(int(x)) if frames[i] > 0 else None)
+            mels.append(m)
+        st = {k: torch.stack([states.get(int(x), zero)[k] for x in sids]) for k in zero}
+        reset = torch.tensor([int(x) not in states for x in sids])
+        raw, soft, _, _, nxt = model.step(torch.from_numpy(np.stack(mels)), torch.ones(n, 8, dtype=torch.bool),
+                                          st, reset)
+        for i, x in enumerate(sids):
+            states[int(x)] = {k: v[i] for k, v in nxt.items()}
+        assert_parity(out["raw"], raw, f"raw step {t}")
+        assert_parity(out["soft"], soft, f"soft step {t}")
+        ref_film = film_ref.film_forward(fw, out["soft"].float().cpu(), query.float())
+        assert_parity(out["film"], ref_film, f"film step {t}", 0.9999, 1e-2)
+    assert eng.status() == 0
+    assert min(sizes) < 16 and max(sizes) > 150, sizes
     eng.close()
 
 

@@ -29,40 +29,20 @@ def _ocfg(cfg):
 def replay_tower(pkg, cfg, g):
     """Drives the oracle through a golden trace; returns (raw, soft, sub, layers) stacked like the golden."""
     from gemma4_omni_b200.synthetic import synthetic_tower_weights
+    from helpers import replay_oracle_trace
 
-    w = {k: torch.from_numpy(v) for k, v in synthetic_tower_weights(cfg, int(g["seed_w"])).items()}
-    model = conformer_ref.OracleConformer(w, _ocfg(cfg))
-    rows = json.loads(str(g["rows"]))
-    reasons = json.loads(str(g["reasons"]))
-    slots = g["slots"]
-    state: dict[int, dict] = {}
-    zero = {k: v[0] for k, v in conformer_ref.zero_state(model.cfg, 1).items()}
-    raws, softs, subs, layers = [], [], [], []
-    off = 0
-    for tick_rows, tick_reasons in zip(rows, reasons):
-        n = len(tick_rows)
-        sl = [int(s) for s in slots[off:off + n]]
-        st = {k: torch.stack([state.get(s, zero)[k] for s in sl]) for k in zero}
-        reset = torch.tensor([r != "continue" for r in tick_reasons])
-        mel = torch.from_numpy(g["mel"][off:off + n])
-        mask = torch.from_numpy(g["mask"][off:off + n])
-        raw, soft, sub, lay, nxt = model.step(mel, mask, st, reset)
-        for i, s in enumerate(sl):
-            state[s] = {k: v[i] for k, v in nxt.items()}
-        raws.append(raw)
-        softs.append(soft)
-        subs.append(sub)
-        layers.append(torch.stack(lay))
-        off += n
-    return torch.cat(raws), torch.cat(softs), torch.cat(subs), torch.cat(layers, dim=1)
+    nontrivial = bool(g["nontrivial"]) if "nontrivial" in g.files else False
+    w = {k: torch.from_numpy(np.asarray(v))
+         for k, v in synthetic_tower_weights(cfg, int(g["seed_w"]), nontrivial=nontrivial).items()}
+    return replay_oracle_trace(conformer_ref.OracleConformer(w, _ocfg(cfg)), g)
 
 
-@pytest.mark.parametrize("fixture", ["tower_tiny", "tower_small"])
+@pytest.mark.parametrize("fixture", ["tower_tiny", "tower_small", "tower_small_nt"])
 def test_oracle_tower_matches_reference_trace(pkg, fixture):
     from gemma4_omni_b200.config import SMALL, ListenerConfig
 
     g = np.load(GOLD / f"{fixture}.npz")
-    cfg = SMALL if fixture == "tower_small" else ListenerConfig(
+    cfg = SMALL if fixture.startswith("tower_small") else ListenerConfig(
         hidden=32, layers=3, heads=4, ffn=128, sub_ch1=4, output_dims=24, text_hidden=24, film_enabled=False)
     raw, soft, sub, layers = replay_tower(pkg, cfg, g)
     torch.testing.assert_close(sub, torch.from_numpy(g["sub"]), rtol=2e-5, atol=2e-6)
@@ -71,10 +51,11 @@ def test_oracle_tower_matches_reference_trace(pkg, fixture):
     torch.testing.assert_close(soft, torch.from_numpy(g["soft"]), rtol=2e-5, atol=2e-5)
 
 
-def test_oracle_full_config_tower_matches_reference(pkg):
+@pytest.mark.parametrize("fixture", ["tower_full", "tower_full_nt"])
+def test_oracle_full_config_tower_matches_reference(pkg, fixture):
     from gemma4_omni_b200.config import FULL
 
-    g = np.load(GOLD / "tower_full.npz")
+    g = np.load(GOLD / f"{fixture}.npz")
     raw, soft, sub, _ = replay_tower(pkg, FULL, g)
     torch.testing.assert_close(sub, torch.from_numpy(g["sub"]), rtol=2e-5, atol=2e-5)
     torch.testing.assert_close(raw, torch.from_numpy(g["raw"]), rtol=1e-4, atol=1e-4)
@@ -95,14 +76,15 @@ def test_oracle_mel_matches_reference_extractor():
     np.testing.assert_array_equal(np.stack(tails), g["tail"])
 
 
-@pytest.mark.parametrize("tag", ["full", "small"])
+@pytest.mark.parametrize("tag", ["full", "small", "full_nt", "small_nt"])
 def test_oracle_film_matches_reference_adapter(pkg, tag):
     from gemma4_omni_b200.config import FULL, SMALL
     from gemma4_omni_b200.synthetic import synthetic_film_weights
 
     g = np.load(GOLD / "film.npz")
-    cfg = FULL if tag == "full" else SMALL
-    w = {k: torch.from_numpy(np.asarray(v)) for k, v in synthetic_film_weights(cfg, 77).items()}
+    cfg = FULL if tag.startswith("full") else SMALL
+    w = {k: torch.from_numpy(np.asarray(v))
+         for k, v in synthetic_film_weights(cfg, 77, nontrivial=tag.endswith("_nt")).items()}
     w["output.weight"] = w["output.weight"] * float(g[f"{tag}_output_weight_scale"])
     y = film_ref.film_forward(w, torch.from_numpy(g[f"{tag}_hidden"]), torch.from_numpy(g[f"{tag}_query"]))
     ref = torch.from_numpy(g[f"{tag}_out"])
@@ -144,3 +126,14 @@ def test_oracle_dispatch_snapshot_matches_reference():
     assert sorted(deferred) == d["deferred0"]
     t1 = packer_ref.snapshot_ready_rows(d["registrations"], paused, ingress, deferred, d["deadline1"])
     assert [f.session_id for f in t1] == d["tick1"]
+
+
+def test_oracle_coordinator_order_matches_reference():
+    """order_ready_heads vs the reference coordinator's take_ready on a seeded
+    enqueue/take trace with every dispatch reason (listener_microbatch.py:170-279)."""
+    from helpers import replay_coordinator
+
+    g = json.loads(str(np.load(GOLD / "packer.npz")["coordinator"]))
+    reasons = {ev["reason"] for ev in g["events"] if ev["kind"] == "take"}
+    assert {"batch_full", "multiple_ready", "coalesce_deadline", None} <= reasons
+    assert replay_coordinator(g, packer_ref.order_ready_heads) > 50
