@@ -15,8 +15,17 @@ FiLM queries, D2H of soft tokens and FiLM outputs inside the timed region).
 Multi-GPU: one process per GPU (torchrun), sessions sharded by id, no
 collective on the step; timings are the max over ranks.
 
-`--impl reference` times the CPU oracle port of the reference path (mel +
-Conformer + FiLM in fp32 on the host cores) on a bounded sample.
+Extra keys of the same line: `latency_e2e` (p50/p99 over 500 end-to-end ticks
+at the benched N), `small_n` (weight-streaming regime, N in {1, 4, 16, 64}:
+step time and achieved HBM GB/s against the step's algorithmic bytes),
+`capacity_sweep` (end-to-end p50/p99 per N; `realtime_sessions_per_gpu` is the
+largest N whose end-to-end p99 < 20 ms), and `config4` (
+8192 sessions in total sharded by session id over the job's GPUs, 2000 steps).
+
+`--impl reference` times the CPU port of the reference path (mel + Conformer +
+FiLM in fp32 on all host cores; the port is pinned to goldens of the
+reference's own classes, which cannot be installed as a package) on a
+bounded sample of the same workload.
 """
 from __future__ import annotations
 
@@ -62,6 +71,9 @@ def parse():
     ap.add_argument("--no-sweep", action="store_true", help="skip the real-time capacity sweep")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--e2e-steps", type=int, default=500, help="end-to-end latency loop length")
+    ap.add_argument("--c4-steps", type=int, default=2000, help="config-4 steps (0: skip)")
+    ap.add_argument("--c4-sessions", type=int, default=8192, help="config-4 sessions over the whole job")
     return ap.parse_args()
 
 
@@ -139,43 +151,79 @@ def workload_config(args, world: int) -> dict:
             "parallelism": f"session-sharded x{world}"}
 
 
-def cpu_baseline(pkg, eff: dict, n_sessions: int, seconds: float):
-    """Times the oracle port (mel + Conformer + FiLM, fp32) on the host cores."""
-    import torch
+def host_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:  # pragma: no cover
+        return os.cpu_count() or 1
 
-    sys.path.insert(0, str(ROOT))
-    from oracle import conformer_ref, film_ref, mel_ref
-    from gemma4_omni_b200 import synthetic
-    from gemma4_omni_b200.config import FULL
 
-    cores = os.cpu_count() or 1
-    torch.set_num_threads(cores)
-    ocfg = conformer_ref.OracleConfig(hidden=FULL.hidden, layers=FULL.layers, heads=FULL.heads, ffn=FULL.ffn)
-    tw = {k: torch.from_numpy(v) for k, v in eff.items() if not k.startswith("film.")}
-    fw = {k[5:]: torch.from_numpy(v) for k, v in eff.items() if k.startswith("film.")}
-    model = conformer_ref.OracleConformer(tw, ocfg)
-    state = conformer_ref.zero_state(ocfg, n_sessions)
-    pcm = np.stack([synthetic.session_audio(99, s, 64, total_frames=64) for s in range(n_sessions)], axis=1)
-    tails = [None] * n_sessions
-    q = torch.randn(n_sessions, 2, FULL.film_query_dim)
-    steps = 0
-    t0 = time.perf_counter()
-    while True:
-        mels = []
-        for i in range(n_sessions):
-            m, tails[i] = mel_ref.extract_single_frame(pcm[steps % 64, i], tails[i])
-            mels.append(m)
-        _, soft, _, _, state = model.step(torch.from_numpy(np.stack(mels)), torch.ones(n_sessions, 8, dtype=torch.bool),
-                                          state, torch.full((n_sessions,), steps == 0))
-        film_ref.film_forward(fw, soft, q)
-        steps += 1
-        el = time.perf_counter() - t0
-        if (el >= seconds and steps >= 2) or steps >= 64:
-            break
-    ms = el / steps * 1e3
-    return {"value": n_sessions * steps / el, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"{steps} steps x {n_sessions} sessions of the d=1536 int8-dequantised tower + mel + FiLM "
-                      f"in fp32 ({ms:.1f} ms/step)", "ms_per_step": ms}
+class CpuPort:
+    """The CPU port of the reference path (oracle/: mel + Conformer + FiLM,
+    fp32 torch on every host core), driven like the serving tick."""
+
+    def __init__(self, eff: dict):
+        import torch
+        sys.path.insert(0, str(ROOT))
+        from oracle import conformer_ref
+        from gemma4_omni_b200.config import FULL
+
+        torch.set_num_threads(host_cores())
+        self.cfg = conformer_ref.OracleConfig(hidden=FULL.hidden, layers=FULL.layers, heads=FULL.heads,
+                                              ffn=FULL.ffn)
+        self.model = conformer_ref.OracleConformer(
+            {k: torch.from_numpy(np.asarray(v)) for k, v in eff.items() if not k.startswith("film.")}, self.cfg)
+        self.film = {k[5:]: torch.from_numpy(np.asarray(v)) for k, v in eff.items() if k.startswith("film.")}
+
+    def time_steps(self, n: int, steps: int, seconds: float) -> tuple[float, int]:
+        """ms per step of n sessions (one untimed warm-up step, then up to
+        `steps` timed steps or `seconds`, at least one)."""
+        import torch
+        from oracle import conformer_ref, film_ref, mel_ref
+        from gemma4_omni_b200 import synthetic
+        from gemma4_omni_b200.config import FULL
+
+        P = 4
+        pcm = np.stack([synthetic.session_audio(99, s, P, total_frames=P) for s in range(n)], axis=1)
+        q = torch.randn(n, 2, FULL.film_query_dim)
+        state = conformer_ref.zero_state(self.cfg, n)
+        tails = [None] * n
+        mask = torch.ones(n, 8, dtype=torch.bool)
+        done, t0 = -1, 0.0
+        while True:
+            if done == 0:
+                t0 = time.perf_counter()
+            mels = []
+            for i in range(n):
+                m, tails[i] = mel_ref.extract_single_frame(pcm[(done + 1) % P, i], tails[i])
+                mels.append(m)
+            _, soft, _, _, state = self.model.step(torch.from_numpy(np.stack(mels)), mask, state,
+                                                   torch.full((n,), done < 0))
+            film_ref.film_forward(self.film, soft, q)
+            done += 1
+            if done >= 1 and (done >= steps or time.perf_counter() - t0 >= seconds):
+                break
+        return (time.perf_counter() - t0) / done * 1e3, done
+
+
+def cpu_baseline(eff: dict, sessions: int, steps: int, seconds: float, ladder: bool) -> dict:
+    """The CPU port on the benched workload (`sessions` concurrent sessions,
+    a bounded number of steps) and, with `ladder`, ms/step at N in {1,2,4,8,16}
+    and the CPU real-time ceiling (largest N with a step under 80 ms)."""
+    port = CpuPort(eff)
+    ms, done = port.time_steps(sessions, steps, seconds)
+    out = {"value": sessions / (ms / 1e3), "unit": UNIT, "cores": host_cores(), "kind": "port",
+           "sample": f"{done} timed steps (+1 warm-up) of the full workload: {sessions} sessions, d=1536 "
+                     f"int8-dequantised tower + mel + FiLM in fp32 ({ms:.1f} ms/step)",
+           "ms_per_step": ms}
+    if ladder:
+        per_n = {}
+        for n in (1, 2, 4, 8, 16):
+            per_n[n] = port.time_steps(n, 20, 2.0)[0]
+        ok = [n for n, v in per_n.items() if v < 80.0]
+        out["ms_per_step_by_n"] = {str(k): round(v, 2) for k, v in per_n.items()}
+        out["realtime_sessions"] = max(ok) if ok else 0
+    return out
 
 
 def synth_weights(pkg, seed=1234):
@@ -192,76 +240,100 @@ def effective_only(pkg, fmt: int, tower, film):
 
 # --------------------------------------------------------------- workload
 class Schedule:
-    """Per-step row arrays for `sessions` lanes, with handle allocation and releases."""
+    """Per-step rows of `sessions` lanes (BASELINE configs 3-4 arrivals): lane l
+    runs sessions back to back, so it is the session's directory handle; the
+    handles of lanes whose session ended are released before the next pack.
+    Global session ids are lane-local ids * id_stride + id_offset, i.e. the ids
+    sharding.shard_of routes to this rank when offset = rank, stride = world."""
 
-    def __init__(self, pkg, sessions: int, steps: int, seed: int, id_offset: int, id_stride: int):
+    def __init__(self, pkg, sessions: int, steps: int, seed: int, id_offset: int = 0, id_stride: int = 1):
         from gemma4_omni_b200 import synthetic
         ar = synthetic.ArrivalProcess(sessions, seed=seed, mode="lanes")
-        free = list(range(sessions - 1, -1, -1))
-        live: dict[int, int] = {}
-        self.rows = []
-        for _ in range(steps):
+        self.n = sessions
+        self.frames = np.empty((steps, sessions), np.int64)
+        self.released: list[np.ndarray] = []
+        self.gids: list[np.ndarray] = []
+        for t in range(steps):
             lanes, sids, frames, new = ar.step()
-            # global session ids gid = id_offset (mod id_stride): with offset = rank
-            # and stride = world these are exactly the ids sharding.shard_of
-            # routes to this rank
-            gids = sids * id_stride + id_offset
-            alive = set(gids.tolist())
-            released = [h for g, h in list(live.items()) if g not in alive]
-            for g in [g for g in live if g not in alive]:
-                free.append(live.pop(g))
-            handles = np.empty(len(gids), np.int32)
-            for i, g in enumerate(gids.tolist()):
-                if g not in live:
-                    live[g] = free.pop()
-                handles[i] = live[g]
-            self.rows.append((handles, np.zeros(len(gids), np.int64), frames.astype(np.int64),
-                              frames.astype(np.int64), released))
+            self.frames[t] = frames
+            self.released.append(lanes[new].astype(np.int32))
+            self.gids.append(sids * id_stride + id_offset)
+        self.handles = np.arange(sessions, dtype=np.int32)
+        self.keys = np.zeros(sessions, np.int64)
+
+    def device(self, device):
+        import torch
+        self.d_handles = torch.from_numpy(self.handles).to(device)
+        self.d_keys = torch.from_numpy(self.keys).to(device)
+        self.d_frames = torch.from_numpy(self.frames).to(device)
+        self.d_released = [torch.from_numpy(r).to(device) for r in self.released]
+        return self
+
+
+def pcm_pool(n: int, P: int, device=None):
+    from gemma4_omni_b200 import synthetic
+    pool = np.stack([synthetic.session_audio(3, s % 4096, P, total_frames=P) for s in range(n)], axis=1)
+    return pool if device is None else __import__("torch").from_numpy(pool).to(device)
+
+
+def device_loop(eng, sched, pcm, query, steps: int, first: int, stream, clocks=None):
+    """`steps` device-resident ticks (release -> pack -> step -> commit) from step
+    `first`; returns (elapsed ms, sorted per-step ms) from CUDA events."""
+    import torch
+    P = pcm.shape[0]
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    b, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    b.record(stream)
+    for i in range(steps):
+        t = first + i
+        starts[i].record(stream)
+        eng.reset_handles(sched.d_released[t])
+        f = sched.d_frames[t]
+        eng.pack(sched.d_handles, sched.d_keys, f, f)
+        eng.step(pcm[t % P], query=query[t % query.shape[0]] if query is not None else None, want_raw=False)
+        eng.commit()
+        ends[i].record(stream)
+    e.record(stream)
+    torch.cuda.synchronize()
+    return b.elapsed_time(e), sorted(s.elapsed_time(x) for s, x in zip(starts, ends))
+
+
+def pct(v, q):
+    return v[min(len(v) - 1, int(q * len(v)))]
 
 
 def run_ours(args, pkg, rank, world, device):
     import torch
-    from gemma4_omni_b200 import _lib, runtime, synthetic
+    from gemma4_omni_b200 import runtime, synthetic
     from gemma4_omni_b200.config import FULL
 
     fmt = 1 if args.weights == "int8" else 0
     n = args.sessions
-    sweep = [] if (args.no_sweep or world > 1) else [256, 1024, 2048, 4096, 8192]
-    cap = max([n] + sweep)
+    one_gpu = world == 1
+    sweep = [] if (args.no_sweep or not one_gpu) else [256, 1024, 2048, 4096, 8192]
+    c4_n = args.c4_sessions // world if args.c4_steps > 0 else 0
+    cap = max([n, c4_n] + sweep)
     eng = runtime.ListenerEngine(FULL, max_sessions=cap, max_rows=cap, max_handles=cap, weight_format=fmt,
                                  device=device)
     tower, film = synth_weights(pkg)
-    eng.load_weights(tower, film, keep_effective=(rank == 0 and not args.no_cpu))
+    eng.load_weights(tower, film, keep_effective=(rank == 0 and one_gpu and not args.no_cpu))
+    stream = torch.cuda.current_stream(device)
+    P = 4
     total = args.warmup + args.steps
-    sched = Schedule(pkg, n, total, seed=7 + rank, id_offset=rank, id_stride=world)
-    P = 8
-    pcm_pool = np.stack([synthetic.session_audio(3, s, P, total_frames=P) for s in range(n)], axis=1)
+    sched = Schedule(pkg, n, total, seed=7 + rank, id_offset=rank, id_stride=world).device(device)
+    pool = pcm_pool(n, P)
+    dev_pcm = torch.from_numpy(pool).to(device)
     q_pool = (torch.randn(2, n, 2, FULL.film_query_dim, generator=torch.Generator().manual_seed(rank))
               .to(torch.bfloat16))
-    # device-resident inputs for the `value` leg
-    dev_rows = [tuple(torch.from_numpy(a).to(device) for a in r[:4]) for r in sched.rows]
-    dev_pcm = torch.from_numpy(pcm_pool).to(device)
     dev_q = q_pool.to(device)
-    stream = torch.cuda.current_stream(device)
 
-    def one_step(t):
-        h, k, f, s = dev_rows[t]
-        for rel in sched.rows[t][4]:
-            eng.reset_handle(rel)
-        eng.pack(h, k, f, s)
-        out = eng.step(dev_pcm[t % P], query=dev_q[t % 2], want_raw=False)
-        eng.commit()
-        return out
-
-    for t in range(args.warmup):
-        one_step(t)
-    torch.cuda.synchronize(device)
+    # ---- warm-up, then the timed region (device-resident inputs)
+    device_loop(eng, sched, dev_pcm, dev_q, args.warmup, 0, stream)
     if eng.status() != 0:
         raise RuntimeError(f"device status {eng.status()} after warm-up")
-    kernels_per_step = eng.lib.lb_step_kernel_count(eng._ctx) + 2  # graph + pack + commit
-    releases = sum(len(sched.rows[t][4]) for t in range(args.warmup, total))
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    kernels_per_step = eng.lib.lb_step_kernel_count(eng._ctx) + 3  # graph + release + pack + commit
     bus = None
     try:
         bus = torch.cuda.get_device_properties(device).pci_bus_id
@@ -271,69 +343,55 @@ def run_ours(args, pkg, rank, world, device):
         torch.distributed.barrier()
     torch.cuda.synchronize(device)
     with ClockSampler(bus) as clk:
-        t_begin = torch.cuda.Event(enable_timing=True)
-        t_end = torch.cuda.Event(enable_timing=True)
-        t_begin.record(stream)
-        for i, t in enumerate(range(args.warmup, total)):
-            starts[i].record(stream)
-            one_step(t)
-            ends[i].record(stream)
-        t_end.record(stream)
-        torch.cuda.synchronize(device)
+        elapsed_ms, lat = device_loop(eng, sched, dev_pcm, dev_q, args.steps, args.warmup, stream)
     if world > 1:
         torch.distributed.barrier()
-    elapsed_ms = t_begin.elapsed_time(t_end)
-    lat = sorted(s.elapsed_time(e) for s, e in zip(starts, ends))
-    status = eng.status()
-    if status != 0:
-        raise RuntimeError(f"device status {status} in the timed region")
+    frames = n * args.steps
+    if eng.status() != 0:
+        raise RuntimeError(f"device status {eng.status()} in the timed region")
+    eng.reset_handles(sched.d_handles)
 
-    # ---- e2e through the C ABI with host buffers (lb_step_host)
-    e2e_steps = min(args.steps, 30)
-    # host buffers in page-locked memory, as a serving process holds its
-    # per-tick PCM and query staging (lb_step_host then DMAs them directly)
+    # ---- end to end through the C ABI with host buffers (lb_step_host), in
+    # page-locked memory as a serving process holds its per-tick staging
     def pinned_np(shape, dtype):
         t = torch.empty(shape, dtype={np.uint16: torch.int16, np.float32: torch.float32}[dtype], pin_memory=True)
         return t.numpy().view(dtype)
-    soft_out = pinned_np((n, 2, FULL.text_hidden), np.uint16)
-    film_out = pinned_np((n, 2, FULL.film_query_dim), np.uint16)
-    q_host = []
-    for i in range(2):
-        q = pinned_np((n, 2, FULL.film_query_dim), np.uint16)
-        q[...] = q_pool[i].view(torch.int16).numpy().view(np.uint16)
-        q_host.append(q)
-    pcm_host = []
-    for i in range(P):
-        buf = pinned_np(pcm_pool[i].shape, np.float32)
-        buf[...] = pcm_pool[i]
-        pcm_host.append(buf)
-    sched2 = Schedule(pkg, n, e2e_steps + 2, seed=1000 + rank, id_offset=rank, id_stride=world)
-    # release every handle of the first schedule so the e2e sessions start clean
-    torch.cuda.synchronize(device)
-    for h in range(cap):
-        eng.reset_handle(h)
-    e2e_lat = []
 
-    def host_step(t):
-        hh, kk, ff, ss, rel = sched2.rows[t]
-        for r in rel:
-            eng.reset_handle(r)
-        eng.step_host(hh, kk, ff, ss, pcm_host[t % P], query=q_host[t % 2], out_soft=soft_out, out_film=film_out)
+    def e2e_run(ns, steps, seed, pcm_np, qs):
+        sc = Schedule(pkg, ns, steps + 2, seed=seed, id_offset=rank, id_stride=world)
+        soft_out = pinned_np((ns, 2, FULL.text_hidden), np.uint16)
+        film_out = pinned_np((ns, 2, FULL.film_query_dim), np.uint16)
+        pcm_h = []
+        for i in range(pcm_np.shape[0]):
+            buf = pinned_np((ns, 1280), np.float32)
+            buf[...] = pcm_np[i][:ns]
+            pcm_h.append(buf)
+        q_h = []
+        for q in qs:
+            buf = pinned_np((ns, 2, FULL.film_query_dim), np.uint16)
+            buf[...] = q[:ns].view(torch.int16).numpy().view(np.uint16)
+            q_h.append(buf)
+        rel_dev = [torch.from_numpy(r).to(device) for r in sc.released]
+        lats = []
+        t_all = 0.0
+        for t in range(steps + 2):
+            a = time.perf_counter()
+            eng.reset_handles(rel_dev[t])
+            eng.step_host(sc.handles, sc.keys, sc.frames[t], sc.frames[t], pcm_h[t % len(pcm_h)],
+                          query=q_h[t % len(q_h)], out_soft=soft_out, out_film=film_out)
+            dt = time.perf_counter() - a
+            if t >= 2:
+                lats.append(dt * 1e3)
+                t_all += dt
+        torch.cuda.synchronize(device)
+        eng.reset_handles(torch.from_numpy(sc.handles).to(device))
+        h2d = int(sc.handles.nbytes + sc.keys.nbytes + 2 * sc.frames[0].nbytes + pcm_h[0].nbytes + q_h[0].nbytes)
+        d2h = int(soft_out.nbytes + film_out.nbytes)
+        return sorted(lats), ns * steps / t_all, h2d, d2h
 
-    host_step(0)
-    host_step(1)
     if world > 1:
         torch.distributed.barrier()
-    t0 = time.perf_counter()
-    for t in range(2, e2e_steps + 2):
-        a = time.perf_counter()
-        host_step(t)
-        e2e_lat.append((time.perf_counter() - a) * 1e3)
-    e2e_s = time.perf_counter() - t0
-    e2e_frames = sum(len(sched2.rows[t][0]) for t in range(2, e2e_steps + 2))
-    h2d = int(np.mean([r[0].nbytes + r[1].nbytes + r[2].nbytes + r[3].nbytes for r in sched2.rows]) +
-              pcm_pool[0].nbytes + q_host[0].nbytes)
-    d2h = soft_out.nbytes + film_out.nbytes
+    e2e_lat, e2e_value, h2d, d2h = e2e_run(n, args.e2e_steps, 1000 + rank, pool, list(q_pool))
 
     # ---- dominant kernel: the FFN1 GEMM at this step's token count, timed alone,
     # with the weight kind the step's bucket uses: int8 codes read as fp16-widened
@@ -342,22 +400,21 @@ def run_ours(args, pkg, rank, world, device):
     w_kind = fmt
     if fmt == 1 and M >= 512 and os.environ.get("LB_INT8_WIDE", "1") != "0":
         w_kind = 2
-    # int8 weights take fp16 activations, bf16 weights bf16 ones (as inside the step)
     x = torch.randn(M, FULL.hidden, device=device).to(torch.float16 if fmt == 1 else torch.bfloat16)
     if fmt == 1:
         wq = torch.randint(-127, 128, (FULL.ffn, FULL.hidden), dtype=torch.int8, device=device)
         if w_kind == 2:
             wq = wq.to(torch.float16)
-        sc = torch.full((FULL.ffn,), 1e-3, dtype=torch.float16, device=device)
+        sc_ = torch.full((FULL.ffn,), 1e-3, dtype=torch.float16, device=device)
     else:
         wq = (torch.randn(FULL.ffn, FULL.hidden, device=device) * 0.02).to(torch.bfloat16)
-        sc = None
+        sc_ = None
     yo = torch.empty(M, FULL.ffn, dtype=torch.bfloat16, device=device)
 
     def gemm():
-        return eng.lib.lb_op_gemm(x.data_ptr(), FULL.hidden, M, wq.data_ptr(), w_kind, None if sc is None else sc.data_ptr(),
-                                  None, FULL.ffn, FULL.hidden, yo.data_ptr(), FULL.ffn, 0, 1, 1, None,
-                                  stream.cuda_stream)
+        return eng.lib.lb_op_gemm(x.data_ptr(), FULL.hidden, M, wq.data_ptr(), w_kind,
+                                  None if sc_ is None else sc_.data_ptr(), None, FULL.ffn, FULL.hidden,
+                                  yo.data_ptr(), FULL.ffn, 0, 1, 1, None, stream.cuda_stream)
     for _ in range(5):
         gemm()
     g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -368,46 +425,69 @@ def run_ours(args, pkg, rank, world, device):
     g1.record(stream)
     torch.cuda.synchronize(device)
     gemm_ms = g0.elapsed_time(g1) / reps
+    del x, wq, yo
 
-    # ---- real-time capacity sweep (1 GPU): largest N with p99 step < 20 ms
+    # ---- weight-streaming regime: small N, device-resident, step time vs the
+    # step's algorithmic bytes (weights + per-session state)
+    small = {}
+    if one_gpu:
+        for ns in (1, 4, 16, 64):
+            sc = Schedule(pkg, ns, 230, seed=300 + ns).device(device)
+            pc = dev_pcm[:, :ns].contiguous()
+            qq = dev_q[:, :ns].contiguous()
+            device_loop(eng, sc, pc, qq, 30, 0, stream)
+            ms_all, lats = device_loop(eng, sc, pc, qq, 200, 30, stream)
+            eng.reset_handles(sc.d_handles)
+            ms = ms_all / 200
+            nbytes = (0.659e9 if fmt == 1 else 1.318e9) + ns * 1.24e6
+            small[str(ns)] = {"ms_per_step": ms, "p50_ms": pct(lats, 0.5), "p99_ms": pct(lats, 0.99),
+                              "frames_per_s": ns / (ms / 1e3), "algorithmic_bytes": nbytes,
+                              "achieved_gbs": nbytes / (ms / 1e3) / 1e9}
+
+    # ---- real-time capacity sweep (1 GPU), end to end: largest N with p99 < 20 ms
     sweep_res = {}
     if sweep:
-        for h in range(cap):
-            eng.reset_handle(h)
+        big_pool = pcm_pool(max(sweep), 2)
+        big_q = [torch.randn(max(sweep), 2, FULL.film_query_dim).to(torch.bfloat16) for _ in range(2)]
         for ns in sweep:
-            sc_rows = Schedule(pkg, ns, 14, seed=50 + ns, id_offset=0, id_stride=1)
-            pcm_s = torch.from_numpy(np.ascontiguousarray(np.resize(pcm_pool[0], (ns, 1280)))).to(device)
-            q_s = torch.randn(ns, 2, FULL.film_query_dim, device=device).to(torch.bfloat16)
-            lats = []
-            for t in range(14):
-                hh, kk, ff, ss, rel = sc_rows.rows[t]
-                for r in rel:
-                    eng.reset_handle(r)
-                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                a.record(stream)
-                eng.pack(*(torch.from_numpy(v).to(device) for v in (hh, kk, ff, ss)))
-                eng.step(pcm_s, query=q_s, want_raw=False)
-                eng.commit()
-                b.record(stream)
-                torch.cuda.synchronize(device)
-                if t >= 4:
-                    lats.append(a.elapsed_time(b))
-            for h in set(int(v) for r in sc_rows.rows for v in r[0]):
-                eng.reset_handle(h)
-            lats.sort()
-            sweep_res[ns] = {"p50_ms": lats[len(lats) // 2], "p99_ms": lats[-1],
-                             "frames_per_s": ns / (statistics.mean(lats) / 1e3)}
+            lats, fps, _, _ = e2e_run(ns, 100, 50 + ns, big_pool, big_q)
+            sweep_res[str(ns)] = {"p50_ms": pct(lats, 0.5), "p99_ms": pct(lats, 0.99), "frames_per_s": fps,
+                                  "steps": 100, "path": "lb_step_host (copies included)"}
+        del big_pool, big_q
         if eng.status() != 0:
             raise RuntimeError("device status error in the sweep")
 
-    cpu = None
-    if rank == 0 and not args.no_cpu:
-        cpu = cpu_baseline(pkg, eng.effective_weights, 16, args.cpu_seconds)
+    # ---- c4_sessions in total, sharded by session id over
+    # the job's ranks (strong scaling), args.c4_steps device-resident steps
+    c4 = None
+    if c4_n:
+        sc = Schedule(pkg, c4_n, args.c4_steps + 5, seed=4000 + rank, id_offset=rank, id_stride=world).device(device)
+        pc = torch.from_numpy(pcm_pool(c4_n, 2)).to(device)
+        qq = torch.randn(2, c4_n, 2, FULL.film_query_dim, device=device).to(torch.bfloat16)
+        device_loop(eng, sc, pc, qq, 5, 0, stream)
+        if world > 1:
+            torch.distributed.barrier()
+        c4_ms, c4_lat = device_loop(eng, sc, pc, qq, args.c4_steps, 5, stream)
+        eng.reset_handles(sc.d_handles)
+        c4 = {"elapsed_ms": c4_ms, "frames": c4_n * args.c4_steps, "p50": pct(c4_lat, 0.5),
+              "p99": pct(c4_lat, 0.99), "sessions_per_gpu": c4_n}
+        del sc, pc, qq
+        if eng.status() != 0:
+            raise RuntimeError("device status error in config 4")
+
+    eff = eng.effective_weights
     eng.close()
-    return dict(elapsed_ms=elapsed_ms, lat=lat, frames=sum(len(sched.rows[t][0]) for t in range(args.warmup, total)),
-                kernels=kernels_per_step, releases=releases, clocks=clk.summary(), e2e_s=e2e_s,
-                e2e_frames=e2e_frames, e2e_lat=sorted(e2e_lat), h2d=h2d, d2h=d2h, gemm_ms=gemm_ms, M=M, w_kind=w_kind,
-                sweep=sweep_res, cpu=cpu)
+    return dict(elapsed_ms=elapsed_ms, lat=lat, frames=frames, kernels=kernels_per_step,
+                clocks=clk.summary(), e2e_value=e2e_value, e2e_lat=e2e_lat, h2d=h2d, d2h=d2h, gemm_ms=gemm_ms, M=M,
+                w_kind=w_kind, sweep=sweep_res, small=small, c4=c4, eff=eff)
+
+
+def step_roofline_ms(n: int, weights: str, peaks: dict) -> float:
+    """BASELINE step roofline: max(N x 2.644 GFLOP / sustained tensor peak,
+    (W + N x 1.24 MB) / HBM peak)."""
+    W = 0.659e9 if weights == "int8" else 1.318e9
+    return 1e3 * max(n * 2.644e9 / (peaks.get("bf16_tflops_sustained", 1390.3) * 1e12),
+                     (W + n * 1.24e6) / (peaks.get("hbm_gbs", 6650.0) * 1e9))
 
 
 def main():
@@ -416,13 +496,14 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    dtype = "int8w-fp16act" if args.weights == "int8" else "bf16w-fp16act"
     if args.impl == "reference":
         if rank != 0:
             return
         tower, film = synth_weights(pkg)
         eff = effective_only(pkg, 1 if args.weights == "int8" else 0, tower, film)
         del tower, film
-        cpu = cpu_baseline(pkg, eff, 16, max(args.cpu_seconds, 10.0))
+        cpu = cpu_baseline(eff, args.sessions, 3, max(args.cpu_seconds, 10.0), ladder=False)
         line = {"impl": "reference", "metric": METRIC, "value": cpu["value"], "unit": UNIT, "n_gpus": args.gpus,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": cpu["ms_per_step"],
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
@@ -440,21 +521,38 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                              device_id=device)
     res = run_ours(args, pkg, rank, world, device)
-    elapsed_ms, e2e_s = res["elapsed_ms"], res["e2e_s"]
-    frames, e2e_frames = res["frames"], res["e2e_frames"]
+    elapsed_ms, frames = res["elapsed_ms"], res["frames"]
+    e2e_value = res["e2e_value"]
+    lat = res["lat"]
+    p50, p99 = pct(lat, 0.5), pct(lat, 0.99)
+    e2e_p50, e2e_p99 = pct(res["e2e_lat"], 0.5), pct(res["e2e_lat"], 0.99)
+    c4 = res["c4"]
+    c4_vals = [c4["elapsed_ms"], c4["p50"], c4["p99"]] if c4 else [0.0, 0.0, 0.0]
+    c4_frames = c4["frames"] if c4 else 0
+    e2e_time = args.sessions * args.e2e_steps / e2e_value
     if world > 1:
         from gemma4_omni_b200 import sharding
-        # whole job: the slowest rank's time, every rank's frames
-        (elapsed_ms, e2e_s), (frames, e2e_frames) = sharding.reduce_over_ranks(
-            [elapsed_ms, e2e_s], [frames, e2e_frames], device=device)
+        # whole job: the slowest rank's times, every rank's frames
+        times, counts = sharding.reduce_over_ranks(
+            [elapsed_ms, e2e_time, p50, p99, e2e_p50, e2e_p99] + c4_vals,
+            [frames, args.sessions * args.e2e_steps, c4_frames], device=device)
+        elapsed_ms, e2e_time, p50, p99, e2e_p50, e2e_p99 = times[:6]
+        c4_vals = times[6:]
+        frames, e2e_frames, c4_frames = counts
+        e2e_value = e2e_frames / e2e_time
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
     if rank != 0:
         return
+    cpu = None
+    if world == 1 and not args.no_cpu and res["eff"] is not None:
+        # after the GPU work and outside any process group: all host cores, N=1 job only
+        cpu = cpu_baseline(res["eff"], args.sessions, 2, args.cpu_seconds, ladder=True)
     from gemma4_omni_b200.config import FULL
     peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
     peak_tf = peaks.get("bf16_tflops", 1590.0)
     peak_src = "measured" if peaks else "fallback"
+    hbm = peaks.get("hbm_gbs", 6650.0)
     value = frames / (elapsed_ms / 1e3)
     ms_step = elapsed_ms / args.steps
     M = res["M"]
@@ -468,39 +566,52 @@ def main():
         # in-kernel widening reads 9.4 MB of int8 codes, fp16 codes 18.9 MB (+ 6.3 MB X)
         traffic = {1: 15.794432e6, 2: 25.478144e6}.get(res["w_kind"])
         traffic_src = "ncu dram__bytes_read.sum + dram__bytes_write.sum, bytes per launch"
-    # whole-step roofline (BASELINE: F = N x 2.644 GFLOP, B = W + N x 1.24 MB)
-    n = args.sessions
-    W = 0.659e9 if args.weights == "int8" else 1.318e9
-    t_roof = max(n * 2.644e9 / (peaks.get("bf16_tflops_sustained", 1390.3) * 1e12),
-                 (W + n * 1.24e6) / (peaks.get("hbm_gbs", 6650.0) * 1e9))
-    lat = res["lat"]
+    t_roof = step_roofline_ms(args.sessions, args.weights, peaks)
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dtype,
         "data": "synthetic (seeded PCM, N(0,0.02) weights, geometric session arrivals)",
         "config": workload_config(args, world),
-        "latency_ms": {"p50": lat[len(lat) // 2], "p99": lat[min(len(lat) - 1, int(0.99 * len(lat)))],
-                       "max": lat[-1]},
+        "latency_ms": {"p50": p50, "p99": p99, "max": lat[-1], "steps": len(lat), "path": "device-resident"},
         "roofline": {"bound": "tensor", "kernel": f"FFN1 GEMM {M}x{FULL.ffn}x{FULL.hidden}, weights "
                      + {0: "bf16", 1: "int8 (widened in-kernel)", 2: "int8 codes widened to fp16"}[res["w_kind"]],
                      "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s", "frac": achieved / peak_tf,
                      "traffic": traffic, "traffic_source": traffic_src,
                      "peak_source": f"{peak_src} bf16 burst (kernel timed alone)"},
-        "roofline_step": {"t_roof_ms": t_roof * 1e3, "t_measured_ms": ms_step, "frac": t_roof * 1e3 / ms_step,
+        "roofline_step": {"t_roof_ms": t_roof, "t_measured_ms": ms_step, "frac": t_roof / ms_step,
                           "definition": "max(N*2.644 GFLOP / sustained bf16 peak, (W + N*1.24 MB) / HBM peak)"},
-        "e2e": {"value": e2e_frames / e2e_s, "unit": UNIT, "h2d_bytes_per_step": res["h2d"],
-                "d2h_bytes_per_step": res["d2h"],
-                "latency_ms": {"p50": res["e2e_lat"][len(res["e2e_lat"]) // 2], "p99": res["e2e_lat"][-1]}},
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": res["h2d"], "d2h_bytes_per_step": res["d2h"],
+                "steps": args.e2e_steps},
+        "latency_e2e_ms": {"p50": e2e_p50, "p99": e2e_p99, "steps": args.e2e_steps,
+                           "path": "lb_step_host, host buffers, copies and release/pack/commit included"},
         "clocks": res["clocks"],
-        "gpu_launches": int(res["kernels"] * args.steps + res["releases"]),
+        "gpu_launches": int(res["kernels"] * args.steps),
         "gpu_launches_per_step": res["kernels"],
     }
+    if res["small"]:
+        for v in res["small"].values():
+            v["hbm_frac"] = v["achieved_gbs"] / hbm
+        line["small_n"] = {"regime": "weight streaming (HBM-bound below ~80 sessions at int8)",
+                           "hbm_peak_gbs": hbm, "per_n": res["small"],
+                           "bytes_definition": "W + N x 1.24 MB per step (weights + per-session state)"}
     if res["sweep"]:
-        ok = [ns for ns, v in res["sweep"].items() if v["p99_ms"] < 20.0]
+        ok = [int(ns) for ns, v in res["sweep"].items() if v["p99_ms"] < 20.0]
         line["realtime_sessions_per_gpu"] = max(ok) if ok else 0
         line["capacity_sweep"] = res["sweep"]
-    if res["cpu"]:
-        line["cpu_baseline"] = {k: res["cpu"][k] for k in ("value", "unit", "cores", "kind", "sample")}
+    if c4:
+        c4_ms, c4_p50, c4_p99 = c4_vals
+        per_gpu = args.c4_sessions // world
+        c4_step = c4_ms / args.c4_steps
+        line["config4"] = {"sessions_total": args.c4_sessions, "sessions_per_gpu": per_gpu, "steps": args.c4_steps,
+                           "frames_per_s": c4_frames / (c4_ms / 1e3), "ms_per_step": c4_step,
+                           "p50_ms": c4_p50, "p99_ms": c4_p99,
+                           "roofline_frac_per_gpu": step_roofline_ms(per_gpu, args.weights, peaks) / c4_step,
+                           "realtime": c4_p99 < 20.0, "scaling": "strong (fixed total sessions)",
+                           "path": "device-resident, max over ranks"}
+    if cpu:
+        line["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        line["cpu_baseline"]["ms_per_step_by_n"] = cpu["ms_per_step_by_n"]
+        line["cpu_baseline"]["realtime_sessions"] = cpu["realtime_sessions"]
     print(json.dumps(line), flush=True)
 
 

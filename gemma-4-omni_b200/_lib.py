@@ -60,6 +60,15 @@ class LbConfig(ctypes.Structure):
     ]
 
 
+class LbCounters(ctypes.Structure):
+    _fields_ = [("struct_size", ctypes.c_uint32), ("api_version", ctypes.c_uint32)] + [
+        (n, ctypes.c_uint64) for n in (
+            "packs", "steps", "commits", "aborts", "rollbacks", "resets", "rows_stepped", "rows_continue",
+            "rows_reset", "rows_gap_or_cursor_mismatch", "rows_identity_reset", "rows_committed",
+            "stale_commits")] + [
+        (n, ctypes.c_int32) for n in ("status", "status_history", "graphs_captured", "reserved")]
+
+
 P = ctypes.c_void_p
 I = ctypes.c_int
 I64 = ctypes.c_int64
@@ -89,6 +98,8 @@ SIGNATURES: dict[str, tuple] = {
     "lb_debug_set_stop": (I, [P, I, I]),
     "lb_step_kernel_count": (I, [P]),
     "lb_debug_read_buffer": (I, [P, ctypes.c_char_p, P, ctypes.c_size_t, P]),
+    "lb_get_counters": (I, [P, ctypes.POINTER(LbCounters), P]),
+    "lb_reset_handles_async": (I, [P, I, P, P]),
     "lb_op_gemm": (I, [P, I, I, P, I, P, P, I, I, P, I, I, I, I, P, P]),
     "lb_op_gemm_clipped": (I, [P, I, I, I, P, I, P, P, I, I, P, I, I, I, I, I, P, P, P, P]),
     "lb_op_gemm_splitk_scratch": (I, [P, I, I, P, I, P, P, I, I, P, I, I, I, P, P]),

@@ -44,6 +44,9 @@ struct lb_ctx {
   size_t pinned_bytes = 0;
   std::vector<std::string> names;
   float qkv_bounds[64][3][4];
+  // host-side call counters (lb_get_counters)
+  unsigned long long n_pack = 0, n_step = 0, n_commit = 0, n_abort = 0, n_rollback = 0, n_reset = 0;
+  unsigned long long rows_stepped = 0;
 };
 
 using namespace lb;
@@ -317,6 +320,7 @@ size_t layout_state(Ctx& c, char* base) {
   auto bso = a.take<int>(R);
   auto cnt = a.take<int>(8);
   auto sta = a.take<int>(8);
+  auto ctr = a.take<unsigned long long>(8);
   auto rh = a.take<int>(R);
   auto rs = a.take<int>(R);
   auto rr = a.take<int>(R);
@@ -338,7 +342,7 @@ size_t layout_state(Ctx& c, char* base) {
     c.handle_exp_seq = hq; c.handle_stamp = hst;
     c.bk_handle_slot = bhs; c.bk_handle_key = bhk; c.bk_handle_exp_frame = bhf;
     c.bk_handle_exp_seq = bhq; c.bk_slot_owner = bso;
-    c.dev_counts = cnt; c.status = sta;
+    c.dev_counts = cnt; c.status = sta; c.dev_ctr = ctr;
     c.row_handle = rh; c.row_slot = rs; c.row_reason = rr; c.row_reset = rst; c.row_mask = rm;
     c.row_replacing = rrep; c.row_mask_in = rmi; c.row_meta = rme; c.row_key = rk; c.row_frame = rf;
     c.row_seq = rq; c.row_exp_frame = ref; c.row_exp_seq = req; c.free_list = fl;
@@ -997,6 +1001,7 @@ int lb_pack_async(lb_ctx* x, int n, const int32_t* handles, const int64_t* keys,
   if (e != cudaSuccess) return LB_ERR_CUDA;
   c.packed_rows = n;
   c.state = 1;
+  x->n_pack += 1;
   return LB_OK;
 }
 
@@ -1089,6 +1094,8 @@ int step_enqueue(lb_ctx* x, int kind, const void* input, const void* query, void
   }
   if (e != cudaSuccess) return LB_ERR_CUDA;
   c.state = 2;
+  x->n_step += 1;
+  x->rows_stepped += static_cast<unsigned long long>(n);
   return LB_OK;
 }
 }  // namespace
@@ -1100,6 +1107,7 @@ int lb_commit_async(lb_ctx* x, void* stream) {
   cudaSetDevice(c.device);
   cudaError_t e = launch_commit(c, static_cast<cudaStream_t>(stream));
   c.state = 3;
+  x->n_commit += 1;
   return err_of(e);
 }
 
@@ -1108,6 +1116,7 @@ int lb_abort(lb_ctx* x) {
   Ctx& c = x->c;
   if (c.state != 1 && c.state != 2) return LB_ERR_STATE;
   c.state = 0;
+  x->n_abort += 1;
   return LB_OK;
 }
 
@@ -1118,6 +1127,7 @@ int lb_rollback_async(lb_ctx* x, void* stream) {
   cudaSetDevice(c.device);
   cudaError_t e = launch_rollback(c, static_cast<cudaStream_t>(stream));
   c.state = 0;
+  x->n_rollback += 1;
   return err_of(e);
 }
 
@@ -1128,7 +1138,19 @@ int lb_reset_handle_async(lb_ctx* x, int32_t handle, void* stream) {
   if (c.state == 1 || c.state == 2) return LB_ERR_STATE;
   cudaSetDevice(c.device);
   c.state = 0;
+  x->n_reset += 1;
   return err_of(launch_reset(c, handle, -1, static_cast<cudaStream_t>(stream)));
+}
+
+int lb_reset_handles_async(lb_ctx* x, int n, const int32_t* handles, void* stream) {
+  if (!x || n < 0 || (n > 0 && !handles)) return LB_ERR_INVALID_ARGUMENT;
+  Ctx& c = x->c;
+  if (n > c.max_handles) return LB_ERR_INVALID_ARGUMENT;
+  if (c.state == 1 || c.state == 2) return LB_ERR_STATE;
+  cudaSetDevice(c.device);
+  c.state = 0;
+  x->n_reset += static_cast<unsigned long long>(n);
+  return err_of(launch_reset_many(c, handles, n, static_cast<cudaStream_t>(stream)));
 }
 
 int lb_reset_slot_async(lb_ctx* x, int32_t slot, void* stream) {
@@ -1138,6 +1160,7 @@ int lb_reset_slot_async(lb_ctx* x, int32_t slot, void* stream) {
   if (c.state == 1 || c.state == 2) return LB_ERR_STATE;
   cudaSetDevice(c.device);
   c.state = 0;
+  x->n_reset += 1;
   return err_of(launch_reset(c, -1, slot, static_cast<cudaStream_t>(stream)));
 }
 
@@ -1154,7 +1177,41 @@ int lb_get_status(lb_ctx* x, int32_t* out, void* stream) {
 int lb_clear_status(lb_ctx* x, void* stream) {
   if (!x) return LB_ERR_INVALID_ARGUMENT;
   cudaSetDevice(x->c.device);
-  return err_of(cudaMemsetAsync(x->c.status, 0, 4, static_cast<cudaStream_t>(stream)));
+  return err_of(launch_clear_status(x->c, static_cast<cudaStream_t>(stream)));
+}
+
+int lb_get_counters(lb_ctx* x, lb_counters* out, void* stream) {
+  if (!x || !out) return LB_ERR_INVALID_ARGUMENT;
+  if (out->struct_size != sizeof(lb_counters) || out->api_version != LB_API_VERSION) return LB_ERR_VERSION;
+  Ctx& c = x->c;
+  cudaSetDevice(c.device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  unsigned long long dev[8] = {};
+  int32_t st[2] = {0, 0};
+  cudaError_t e = cudaMemcpyAsync(dev, c.dev_ctr, sizeof(dev), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(st, c.status, sizeof(st), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return LB_ERR_CUDA;
+  out->packs = x->n_pack;
+  out->steps = x->n_step;
+  out->commits = x->n_commit;
+  out->aborts = x->n_abort;
+  out->rollbacks = x->n_rollback;
+  out->resets = x->n_reset;
+  out->rows_stepped = x->rows_stepped;
+  out->rows_continue = dev[0];
+  out->rows_reset = dev[1];
+  out->rows_gap_or_cursor_mismatch = dev[2];
+  out->rows_identity_reset = dev[3];
+  out->rows_committed = dev[4];
+  out->stale_commits = dev[5];
+  out->status = st[0];
+  out->status_history = st[0] | st[1];
+  int graphs = 0;
+  for (auto& p : x->plans)
+    for (auto g : p.graph) graphs += g != nullptr;
+  out->graphs_captured = graphs;
+  return LB_OK;
 }
 
 int lb_read_rows(lb_ctx* x, int32_t* slots, int32_t* reasons, int n, void* stream) {

@@ -67,7 +67,15 @@ struct PackArgs {
   int* free_list;
   int* counts;
   int* status;
+  unsigned long long* ctr;
 };
+
+// Adds this warp's active lanes' votes for `pred` to *dst with one atomic.
+__device__ __forceinline__ void warp_count(bool pred, unsigned long long* dst) {
+  const unsigned am = __activemask();
+  const unsigned votes = __ballot_sync(am, pred);
+  if ((threadIdx.x & 31) == __ffs(am) - 1 && votes) atomicAdd(dst, static_cast<unsigned long long>(__popc(votes)));
+}
 
 __global__ void __launch_bounds__(kPackThreads) pack_kernel(PackArgs a) {
   __shared__ int sh[32];
@@ -152,8 +160,11 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(PackArgs a) {
   // ---- phase 4: effective canonical meta and staged meta per row
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     const int slot = a.row_slot[i];
-    const int reset = a.row_reason[i] != 0;
+    const int reason = a.row_reason[i];
+    const int reset = reason != 0;
     a.row_reset[i] = reset;
+#pragma unroll
+    for (int r = 0; r < 4; ++r) warp_count(reason == r, a.ctr + r);
     if (slot < 0) continue;
     SlotMeta m = a.meta_canon[slot];
     if (reset) {
@@ -196,6 +207,7 @@ struct CommitArgs {
   long long *bk_handle_key, *bk_handle_exp_frame, *bk_handle_exp_seq;
   int* bk_slot_owner;
   int* status;
+  unsigned long long* ctr;
 };
 
 __global__ void __launch_bounds__(kPackThreads) commit_kernel(CommitArgs a) {
@@ -213,7 +225,10 @@ __global__ void __launch_bounds__(kPackThreads) commit_kernel(CommitArgs a) {
   __syncthreads();
   if (stale) {
     if (threadIdx.x == 0) {
-      if (a.counts[3]) atomicOr(a.status, kStatusStaleCommit);
+      if (a.counts[3]) {
+        atomicOr(a.status, kStatusStaleCommit);
+        a.ctr[5] += 1;
+      }
       a.counts_w[2] = 0;
       a.counts_w[3] = 0;
     }
@@ -239,6 +254,7 @@ __global__ void __launch_bounds__(kPackThreads) commit_kernel(CommitArgs a) {
   if (threadIdx.x == 0) {
     a.counts_w[2] = n;
     a.counts_w[3] = 0;  // the packed rows are consumed
+    a.ctr[4] += static_cast<unsigned long long>(n);
   }
 }
 
@@ -302,7 +318,42 @@ CommitArgs commit_args(Ctx& c) {
   a.bk_handle_exp_seq = c.bk_handle_exp_seq;
   a.bk_slot_owner = c.bk_slot_owner;
   a.status = c.status;
+  a.ctr = c.dev_ctr;
   return a;
+}
+
+// Releases n handles at once (sessions that left this tick): each handle's
+// slot is freed and its directory entry cleared, as reset_kernel does for one.
+// Handles are distinct in a well-formed call; an out-of-range one sets
+// kStatusBadHandle and is skipped.
+__global__ void reset_many_kernel(const int* handles, int n, int max_handles, int* handle_slot,
+                                  long long* handle_key, long long* handle_exp_frame,
+                                  long long* handle_exp_seq, int* slot_owner, SlotMeta* meta_canon,
+                                  int* status) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const int h = handles[i];
+    if (h < 0 || h >= max_handles) {
+      atomicOr(status, kStatusBadHandle);
+      continue;
+    }
+    const int slot = handle_slot[h];
+    handle_slot[h] = -1;
+    handle_key[h] = -1;
+    handle_exp_frame[h] = -1;
+    handle_exp_seq[h] = -1;
+    if (slot >= 0) {
+      slot_owner[slot] = -1;
+      meta_canon[slot] = SlotMeta{0, 0, 0, 0};
+    }
+  }
+}
+
+// status[1] |= status[0]; status[0] = 0 (the history keeps every cleared error)
+__global__ void clear_status_kernel(int* status) {
+  if (threadIdx.x == 0) {
+    status[1] |= status[0];
+    status[0] = 0;
+  }
 }
 
 }  // namespace
@@ -337,7 +388,22 @@ cudaError_t launch_pack(Ctx& c, int n_rows, long long step_id, cudaStream_t s) {
   a.free_list = c.free_list;
   a.counts = c.dev_counts;
   a.status = c.status;
+  a.ctr = c.dev_ctr;
   pack_kernel<<<1, kPackThreads, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_reset_many(Ctx& c, const int* handles, int n, cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  const int blocks = (n + 255) / 256 < 64 ? (n + 255) / 256 : 64;
+  reset_many_kernel<<<blocks, 256, 0, s>>>(handles, n, c.max_handles, c.handle_slot, c.handle_key,
+                                           c.handle_exp_frame, c.handle_exp_seq, c.slot_owner,
+                                           c.meta_canon, c.status);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_clear_status(Ctx& c, cudaStream_t s) {
+  clear_status_kernel<<<1, 32, 0, s>>>(c.status);
   return cudaGetLastError();
 }
 

@@ -178,7 +178,11 @@ struct Ctx {
   int* bk_prev_handle_slot = nullptr;
   // per-step rows
   int* dev_counts = nullptr;  // [0] n_rows, [1] n_tok, [2] committed rows, [3] packed flag
-  int* status = nullptr;      // device status word
+  int* status = nullptr;      // device status word; status[1]: OR of every cleared status
+  // running device counters (lb_get_counters): [0..3] packed rows per reset
+  // reason (continue, reset, gap_or_cursor_mismatch, identity_reset), [4] rows
+  // installed by commits, [5] commits refused by the cursor check
+  unsigned long long* dev_ctr = nullptr;
   int *row_handle = nullptr, *row_slot = nullptr, *row_reason = nullptr, *row_reset = nullptr;
   int *row_mask = nullptr, *row_replacing = nullptr;
   uint8_t* row_mask_in = nullptr;  // caller's uint8 masks (copied per step)
@@ -239,6 +243,8 @@ cudaError_t launch_pack(Ctx& c, int n_rows, long long step_id, cudaStream_t s);
 cudaError_t launch_commit(Ctx& c, cudaStream_t s);
 cudaError_t launch_rollback(Ctx& c, cudaStream_t s);
 cudaError_t launch_reset(Ctx& c, int handle, int slot, cudaStream_t s);
+cudaError_t launch_clear_status(Ctx& c, cudaStream_t s);
+cudaError_t launch_reset_many(Ctx& c, const int* handles, int n, cudaStream_t s);
 cudaError_t run_layers(Ctx& c, const Bucket& b, cudaStream_t s);
 
 struct RowFusedArgs {

@@ -154,6 +154,15 @@ class ListenerEngine:
     def reset_handle(self, handle: int) -> None:
         _lib.check("lb_reset_handle_async", self.lib.lb_reset_handle_async(self._ctx, int(handle), self._stream))
 
+    def reset_handles(self, handles: torch.Tensor) -> None:
+        """Releases every handle of an int32 device tensor in one launch."""
+        if handles.dtype != torch.int32 or not handles.is_contiguous() or handles.device != self.device:
+            raise ValueError("handles must be a contiguous int32 tensor on the engine's device")
+        n = int(handles.numel())
+        if n:
+            _lib.check("lb_reset_handles_async",
+                       self.lib.lb_reset_handles_async(self._ctx, n, handles.data_ptr(), self._stream))
+
     def reset_slot(self, slot: int) -> None:
         _lib.check("lb_reset_slot_async", self.lib.lb_reset_slot_async(self._ctx, int(slot), self._stream))
 
@@ -162,6 +171,15 @@ class ListenerEngine:
         v = ctypes.c_int32(0)
         _lib.check("lb_get_status", self.lib.lb_get_status(self._ctx, ctypes.addressof(v), self._stream))
         return int(v.value)
+
+    def counters(self) -> dict[str, int]:
+        """lb_get_counters as a dict (synchronises the current stream)."""
+        c = _lib.LbCounters()
+        c.struct_size = ctypes.sizeof(_lib.LbCounters)
+        c.api_version = 1
+        _lib.check("lb_get_counters", self.lib.lb_get_counters(self._ctx, ctypes.byref(c), self._stream))
+        return {name: int(getattr(c, name)) for name, _ in _lib.LbCounters._fields_
+                if name not in ("struct_size", "api_version", "reserved")}
 
     def clear_status(self) -> None:
         _lib.check("lb_clear_status", self.lib.lb_clear_status(self._ctx, self._stream))

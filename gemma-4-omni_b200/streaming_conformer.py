@@ -15,7 +15,14 @@ state and capacity).
 
 What differs, by design:
 - the slot policy, cache staging and commit run on the GPU (one packer kernel,
-  ring-head commits); slot ids and reasons are read back lazily;
+  ring-head commits); slot ids and reasons are read back lazily, and
+  ``prepare_batch`` does not wait for the step (the host-side checks that
+  precede it are the reference's own capacity and identity rules); the one
+  host wait is in ``commit``, which reads the device's all-or-nothing cursor
+  check -- by then the caller has already waited for the step's outputs;
+- ``prepare_batch_pcm`` takes the 80 ms PCM frames themselves ([N,1280]
+  float32) and runs the log-mel frontend on the GPU with each session's
+  160-sample tail kept in its slot (committed with the rest of its state);
 - one CUDA graph per power-of-two row bucket with a device-side row count
   replaces one graph per N; ``capture_graph`` is accepted and is a no-op;
 - per-layer outputs (``layer_tokens``) and ``subsampled`` cost an eager
@@ -37,6 +44,7 @@ from .runtime import ListenerEngine
 MEL_TICK_ROWS = 8
 MEL_BINS = 128
 Q2_TOKENS = 2
+PCM_SAMPLES = 1280
 REASONS = _lib.REASONS
 
 
@@ -191,7 +199,11 @@ class StreamingConformerAudioTower:
         self._lock = threading.RLock()
         self._closed = False
         self._active: PreparedStreamingAudioBatch | None = None
-        self._handles: dict[str, int] = {}          # session id -> handle
+        # session id -> handle of the device-side session directory; a handle is
+        # returned to the pool when its session's state is released (reset,
+        # reset_session) or when the batch that introduced it is aborted, so
+        # the pool never runs dry under session churn
+        self._handles: dict[str, int] = {}
         self._free_handles: list[int] = list(range(self._engine.max_handles - 1, -1, -1))
         self._key_ids: dict[tuple[int, str], int] = {}  # (generation, epoch) -> int64 key
         self._identity: dict[str, tuple[int, str]] = {}  # committed identity per bound session
@@ -223,6 +235,9 @@ class StreamingConformerAudioTower:
                                     capture_cuda_graphs=True, optimize_cuda=True, **kw)
 
     def _validate_model(self) -> None:
+        """The reference's checks (streaming_conformer.py:375-407): exact chunking,
+        eval mode, modules already on the requested device and dtype, and the
+        subsampler geometry the streaming state layout assumes."""
         config = self.audio_tower.config
         exact = {"attention_chunk_size": 12, "attention_context_left": 13, "attention_context_right": 0,
                  "conv_kernel_size": 5}
@@ -236,6 +251,21 @@ class StreamingConformerAudioTower:
             raise ValueError("Gemma audio layer count differs from its configuration")
         if self.audio_tower.training or self.embed_audio.training:
             raise ValueError("incremental Gemma audio tower requires eval mode")
+        parameter = next(self.audio_tower.parameters())
+        embed_parameter = next(self.embed_audio.parameters())
+        if parameter.device != self.device or embed_parameter.device != self.device:
+            raise ValueError("audio tower and embed_audio must already be on the requested device")
+        if parameter.dtype != self.dtype or embed_parameter.dtype != self.dtype:
+            raise ValueError("audio tower and embed_audio must already use the requested dtype")
+        layers = self.audio_tower.subsample_conv_projection
+        for name in ("layer0", "layer1"):
+            layer = getattr(layers, name, None)
+            if layer is None or tuple(layer.conv.kernel_size) != (3, 3):
+                raise ValueError("Gemma audio subsampler must use its 3x3 convolution layers")
+            if tuple(layer.conv.stride) != (2, 2) or tuple(layer.conv.padding) != (1, 1):
+                raise ValueError("Gemma audio subsampler must use stride 2 and symmetric padding 1")
+            if layer.conv.bias is not None:
+                raise ValueError("Gemma audio subsampler convolutions must remain biasless")
 
     # --------------------------------------------------------------- state
     @property
@@ -268,6 +298,7 @@ class StreamingConformerAudioTower:
             self._engine.reset_handle(self._handles[session_id])
             self._bound.discard(session_id)
             self._identity.pop(session_id, None)
+            self._release_handle(session_id)
             self._last_commit = None
 
     def reset_session(self, slot_idx: int) -> None:
@@ -281,11 +312,12 @@ class StreamingConformerAudioTower:
             if self._active is not None:
                 raise RuntimeError("cannot reset a streaming audio slot while a batch is prepared")
             slot, _, _, _ = self._engine.read_handles()
-            for sid, h in self._handles.items():
-                if slot[h] == slot_idx:
-                    self._bound.discard(sid)
-                    self._identity.pop(sid, None)
+            owners = [sid for sid, h in self._handles.items() if slot[h] == slot_idx]
             self._engine.reset_slot(slot_idx)
+            for sid in owners:
+                self._bound.discard(sid)
+                self._identity.pop(sid, None)
+                self._release_handle(sid)
             self._last_commit = None
 
     def capture_graph(self, batch_size: int) -> None:
@@ -303,6 +335,13 @@ class StreamingConformerAudioTower:
             self._handles[sid] = h
         return h
 
+    def _release_handle(self, sid: str) -> None:
+        """Returns a session's handle to the pool; its directory entry is clear
+        (never committed, or cleared by the reset kernel)."""
+        h = self._handles.pop(sid, None)
+        if h is not None:
+            self._free_handles.append(h)
+
     def prepare_batch(self, mel_tick: torch.Tensor, cursors: Sequence[AudioStreamCursor], *,
                       input_mask: torch.Tensor | None = None, use_cuda_graph: bool = False,
                       graph_event_pair: tuple[Any, Any] | None = None) -> PreparedStreamingAudioBatch:
@@ -314,6 +353,32 @@ class StreamingConformerAudioTower:
             raise ValueError("streaming Q2 Mel input must match [N,8,128] cursors")
         if mel_tick.device != self.device:
             raise ValueError("streaming Q2 Mel input device/dtype differs from the audio tower")
+        return self._prepare(mel_tick.to(torch.float32).contiguous(), _lib.LB_INPUT_MEL, rows, input_mask,
+                             graph_event_pair)
+
+    def prepare_batch_pcm(self, pcm_frames: torch.Tensor, cursors: Sequence[AudioStreamCursor], *,
+                          input_mask: torch.Tensor | None = None,
+                          graph_event_pair: tuple[Any, Any] | None = None) -> PreparedStreamingAudioBatch:
+        """``prepare_batch`` from the raw 80 ms PCM frames ([N,1280] float32, 16 kHz).
+
+        The incremental log-mel of each row (duplex_kernel/listener.py:1807-1850:
+        [160-sample tail | 1280 samples], 8 Hann-windowed 320-sample frames, hop
+        160, |rfft 512|, HTK mel 128, log(x + 1e-3)) runs on the GPU inside the
+        step; the tail lives in the session's slot, advances on ``commit`` and
+        starts from zeros on every reset reason, exactly when the tower state does.
+        """
+        rows = tuple(cursors)
+        if not isinstance(pcm_frames, torch.Tensor) or pcm_frames.ndim != 2:
+            raise ValueError("streaming PCM input must be [N,1280]")
+        n = len(rows)
+        if n <= 0 or tuple(pcm_frames.shape) != (n, PCM_SAMPLES):
+            raise ValueError("streaming PCM input must match [N,1280] cursors")
+        if pcm_frames.device != self.device or pcm_frames.dtype != torch.float32:
+            raise ValueError("streaming PCM input must be float32 on the audio device")
+        return self._prepare(pcm_frames.contiguous(), _lib.LB_INPUT_PCM, rows, input_mask, graph_event_pair)
+
+    def _prepare(self, inputs: torch.Tensor, kind: int, rows: tuple, input_mask, graph_event_pair):
+        n = len(rows)
         if len({row.key for row in rows}) != n or len({row.session_id for row in rows}) != n:
             raise ValueError("a streaming audio batch requires distinct session identities")
         if input_mask is not None and (not isinstance(input_mask, torch.Tensor)
@@ -339,21 +404,21 @@ class StreamingConformerAudioTower:
                 bits = (input_mask.to(torch.uint8) << torch.arange(8, device=self.device, dtype=torch.uint8)).sum(1)
                 masks = bits.to(torch.uint8).contiguous()
             dev = self.device
-            self._engine.pack(handles.to(dev), keys.to(dev), frames.to(dev), seqs.to(dev), masks)
-            if graph_event_pair is not None:
-                graph_event_pair[0].record()
             try:
-                out = self._engine.step(mel_tick.to(torch.float32).contiguous(), kind=_lib.LB_INPUT_MEL,
-                                        debug=self._return_layers)
+                self._engine.pack(handles.to(dev, non_blocking=True), keys.to(dev, non_blocking=True),
+                                  frames.to(dev, non_blocking=True), seqs.to(dev, non_blocking=True), masks)
+                if graph_event_pair is not None:
+                    graph_event_pair[0].record()
+                try:
+                    out = self._engine.step(inputs, kind=kind, debug=self._return_layers)
+                except BaseException:
+                    self._engine.abort()
+                    raise
             except BaseException:
-                self._engine.abort()
+                self._release_new_handles(rows)
                 raise
             if graph_event_pair is not None:
                 graph_event_pair[1].record()
-            if self._engine.status() & (_lib.DEV_SLOT_EXHAUSTED | _lib.DEV_DUPLICATE_ROW | _lib.DEV_BAD_HANDLE):
-                self._engine.abort()
-                self._engine.clear_status()
-                raise RuntimeError(f"streaming audio session bank exhausted ({self.max_sessions} sessions)")
             layers = tuple(out["layers"][i].to(self.dtype) for i in range(self.num_layers)) if self._return_layers else ()
             sub = out["subsampled"].to(self.dtype) if self._return_layers else None
             prepared = PreparedStreamingAudioBatch(
@@ -363,17 +428,31 @@ class StreamingConformerAudioTower:
             self._active = prepared
             return prepared
 
+    def _release_new_handles(self, rows) -> None:
+        """Handles of sessions this (aborted) batch introduced go back to the pool."""
+        for r in rows:
+            if r.session_id not in self._bound:
+                self._release_handle(r.session_id)
+
     def _commit(self, batch: PreparedStreamingAudioBatch) -> None:
         with self._lock:
             if self._active is not batch:
                 raise RuntimeError("streaming audio transaction is no longer active")
             self._active = None
             self._engine.commit()
+            # the one host wait of a tick: the device's all-or-nothing cursor
+            # check (and the packer's capacity / identity checks) of this batch
             st = self._engine.status()
             if st & _lib.DEV_STALE_COMMIT:
                 self._engine.clear_status()
                 batch._aborted = True
+                self._release_new_handles(batch.cursors)
                 raise RuntimeError("cursor changed before streaming commit")
+            if st & (_lib.DEV_SLOT_EXHAUSTED | _lib.DEV_DUPLICATE_ROW | _lib.DEV_BAD_HANDLE):
+                self._engine.clear_status()
+                batch._aborted = True
+                self._release_new_handles(batch.cursors)
+                raise RuntimeError(f"streaming audio session bank exhausted ({self.max_sessions} sessions)")
             if st:
                 raise RuntimeError(f"listener device status {st:#x}")
             prev = (set(self._bound), dict(self._identity))
@@ -390,6 +469,8 @@ class StreamingConformerAudioTower:
             self._engine.rollback()
             self._bound, self._identity = self._last_commit[1]
             self._last_commit = None
+            # sessions the rolled-back batch had introduced are unbound again
+            self._release_new_handles(batch.cursors)
 
     def _abort(self, batch: PreparedStreamingAudioBatch) -> None:
         with self._lock:
@@ -397,6 +478,7 @@ class StreamingConformerAudioTower:
                 raise RuntimeError("streaming audio transaction is no longer active")
             self._active = None
             self._engine.abort()
+            self._release_new_handles(batch.cursors)
 
     def close(self) -> None:
         """Release session state when idle."""

@@ -169,6 +169,11 @@ int lb_rollback_async(lb_ctx* ctx, void* stream);
 /* Releases one session handle (its slot becomes free, state logically zero).
  * StreamingConformerAudioTower.reset (streaming_conformer.py:418-434). */
 int lb_reset_handle_async(lb_ctx* ctx, int32_t handle, void* stream);
+/* Releases n distinct handles (int32 device array) in one launch: the
+ * sessions that left this tick (close_session -> reset for each,
+ * listener_microbatch_frontend.py:363-377, streaming_conformer.py:418-434).
+ * An out-of-range handle sets LB_DEV_BAD_HANDLE and is skipped. */
+int lb_reset_handles_async(lb_ctx* ctx, int n, const int32_t* handles, void* stream);
 /* Releases one slot (StreamingConformerAudioTower.reset_session, :436-451). */
 int lb_reset_slot_async(lb_ctx* ctx, int32_t slot, void* stream);
 
@@ -177,7 +182,30 @@ int lb_step_kernel_count(lb_ctx* ctx);
 
 /* Synchronous reads (they synchronise the given stream). */
 int lb_get_status(lb_ctx* ctx, int32_t* status_out, void* stream);
+/* Asynchronous: clears the status word, keeping its bits in the history
+ * that lb_get_counters reports. */
 int lb_clear_status(lb_ctx* ctx, void* stream);
+
+/* Running per-context counters (the native batch ABI's get_counters,
+ * native/gemma4_listener_microbatch/gemma4_listener_microbatch.h:206-480).
+ * Call counts are kept on the host; the per-reason row counts (every row a
+ * pack resolved, by lb_row_reason), committed rows and refused commits are
+ * kept on the device by the packer / commit kernels.  Set struct_size and
+ * api_version before the call; synchronises `stream`. */
+typedef struct lb_counters {
+  uint32_t struct_size;
+  uint32_t api_version;
+  uint64_t packs, steps, commits, aborts, rollbacks, resets;
+  uint64_t rows_stepped;                 /* sum of the row counts of every step */
+  uint64_t rows_continue, rows_reset, rows_gap_or_cursor_mismatch, rows_identity_reset;
+  uint64_t rows_committed;               /* rows installed by successful commits */
+  uint64_t stale_commits;                /* commits refused by the cursor check */
+  int32_t status;                        /* current device status word */
+  int32_t status_history;                /* OR of every status word since creation */
+  int32_t graphs_captured;               /* CUDA graphs instantiated so far */
+  int32_t reserved;
+} lb_counters;
+int lb_get_counters(lb_ctx* ctx, lb_counters* out, void* stream);
 /* Last packed rows: slot ids and reasons (lb_row_reason). */
 int lb_read_rows(lb_ctx* ctx, int32_t* slots_host, int32_t* reasons_host, int n, void* stream);
 /* Directory dump: per handle slot (-1 = none), key, expected frame / seq. */

@@ -24,6 +24,8 @@ Fixtures:
   tower_full_nt.npz  the config-0 tower with non-identity parameters over the
                      first 18 ticks of the 3-session trace (reorder, cursor gap,
                      epoch change, input masks)
+  pcm_tower_nt.npz   PCM -> _extract_single_frame -> StreamingConformerAudioTower
+                     (SMALL, non-identity parameters), 3 sessions x 12 ticks
   film.npz           FrameResidualQueryFiLMAdapter (1536/2048/256 and the SMALL dims),
                      default and non-identity LayerNorm parameters
   packer.npz         slot ids / reasons / committed positions of the tower's slot
@@ -154,6 +156,43 @@ def run_tower(pkg, cfg, seed_w: int, seed_trace: int, kind: str, nontrivial: boo
         soft=np.concatenate(softs), sub=np.concatenate(subs), slots=np.concatenate(slots),
         layers=np.concatenate(layers, axis=1))
     return out
+
+
+def make_pcm_tower(pkg):
+    """PCM -> the reference's incremental mel (_extract_single_frame, tail carried
+    per session) -> StreamingConformerAudioTower (SMALL, non-identity bf16
+    parameters), 3 sessions over 12 ticks with a late join and a reorder."""
+    from transformers.models.gemma4.feature_extraction_gemma4 import Gemma4AudioFeatureExtractor
+    from duplex_kernel.listener import GemmaAudioTowerBackend
+    from duplex_kernel.streaming_conformer import AudioStreamCursor, StreamingConformerAudioTower
+    from gemma4_omni_b200.config import SMALL
+    from gemma4_omni_b200.synthetic import session_audio, synthetic_tower_weights
+
+    shim = SimpleNamespace(feature_extractor=Gemma4AudioFeatureExtractor())
+    tower, embed = build_reference_tower(SMALL, synthetic_tower_weights(SMALL, 35, nontrivial=True))
+    st = StreamingConformerAudioTower(tower, embed, device="cpu", dtype=torch.float32, max_sessions=4)
+    audio = {s: session_audio(11, i, 12, total_frames=12) for i, s in enumerate(("u", "v", "w"))}
+    tails, frames = {}, {"u": 0, "v": 0, "w": 0}
+    rows_meta, pcms, softs, raws = [], [], [], []
+    with torch.inference_mode():
+        for t in range(12):
+            sids = ["u", "v"] if t < 3 else (["w", "u", "v"] if t % 2 else ["u", "v", "w"])
+            pcm = np.stack([audio[s][frames[s]] for s in sids])
+            mels = []
+            for i, s in enumerate(sids):
+                m, tails[s] = GemmaAudioTowerBackend._extract_single_frame(shim, pcm[i], tails.get(s))
+                mels.append(m)
+            cursors = tuple(AudioStreamCursor(s, 0, "e0", frames[s], frames[s]) for s in sids)
+            p = st.prepare_batch(torch.from_numpy(np.stack(mels)), cursors)
+            raws.append(p.raw_tokens.numpy().copy())
+            softs.append(p.soft_tokens.numpy().copy())
+            p.commit()
+            rows_meta.append([[s, 0, "e0", frames[s]] for s in sids])
+            pcms.append(pcm)
+            for s in sids:
+                frames[s] += 1
+    return {"seed_w": 35, "nontrivial": np.bool_(True), "rows": json.dumps(rows_meta),
+            "pcm": np.concatenate(pcms), "raw": np.concatenate(raws), "soft": np.concatenate(softs)}
 
 
 def make_mel(pkg):
@@ -376,6 +415,7 @@ def main() -> None:
         "tower_full": lambda: full_tower(41, 125, "full"),
         "tower_small_nt": lambda: run_tower(pkg, SMALL, 33, 713, "small", nontrivial=True),
         "tower_full_nt": lambda: full_tower(43, 126, "full_nt", nontrivial=True),
+        "pcm_tower_nt": lambda: make_pcm_tower(pkg),
     }
     unknown = only - set(makers)
     if unknown:

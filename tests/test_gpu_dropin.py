@@ -14,7 +14,7 @@ from oracle import conformer_ref
 pytestmark = pytest.mark.gpu
 
 
-def hf_modules(cfg, seed):
+def hf_modules(cfg, seed, nontrivial=True):
     from gemma4_omni_b200.synthetic import synthetic_tower_weights
     from transformers.models.gemma4 import modeling_gemma4
     from transformers.models.gemma4.configuration_gemma4 import Gemma4AudioConfig, Gemma4TextConfig
@@ -27,10 +27,14 @@ def hf_modules(cfg, seed):
                                            "rope_theta": 1_000_000.0})
     tower = modeling_gemma4.Gemma4AudioModel(ac).eval()
     embed = modeling_gemma4.Gemma4MultimodalEmbedder(ac, tc).eval()
-    w = synthetic_tower_weights(cfg, seed)
-    tower.load_state_dict({k: torch.from_numpy(v) for k, v in w.items() if not k.startswith("embed.")}, strict=False)
+    w = synthetic_tower_weights(cfg, seed, nontrivial=nontrivial)
+    missing, _ = tower.load_state_dict({k: torch.from_numpy(np.asarray(v)) for k, v in w.items()
+                                        if not k.startswith("embed.")}, strict=False)
+    if nontrivial:  # every clip bound is set; only the rel-pos timescales are derived
+        assert all("inv_timescales" in k for k in missing), missing
     embed.load_state_dict({k[6:]: torch.from_numpy(v) for k, v in w.items() if k.startswith("embed.")})
-    return tower, embed, w
+    # the reference tower requires its modules on the serving device and dtype already
+    return tower.to("cuda", torch.bfloat16), embed.to("cuda", torch.bfloat16), w
 
 
 @pytest.fixture(scope="module")
@@ -168,7 +172,7 @@ def test_layer_tokens_match_oracle_with_masks(modules, pkg):
 
     st = tower(modules, 4, layers=True)
     _, _, w = modules
-    eff = {k: torch.from_numpy(bf16_round(v)) for k, v in w.items()}
+    eff = {k: torch.from_numpy(bf16_round(np.asarray(v))) for k, v in w.items()}
     model = conformer_ref.OracleConformer(eff, oracle_config(SMALL))
     state = conformer_ref.zero_state(model.cfg, 1)
     g = torch.Generator().manual_seed(712)
@@ -185,3 +189,210 @@ def test_layer_tokens_match_oracle_with_masks(modules, pkg):
         assert_parity(p.raw_tokens, raw, f"raw {f}")
         p.commit()
     st.close()
+
+
+def test_validation_matches_reference_contract(modules):
+    """Device, dtype, eval-mode and subsampler-geometry checks of the reference
+    (streaming_conformer.py:375-407)."""
+    from gemma4_omni_b200.streaming_conformer import StreamingConformerAudioTower
+    t, e, _ = modules
+    with pytest.raises(ValueError, match="requested dtype"):
+        StreamingConformerAudioTower(t, e, device="cuda", dtype=torch.float32, max_sessions=4)
+    with pytest.raises(ValueError, match="CUDA only"):
+        StreamingConformerAudioTower(t, e, device="cpu", dtype=torch.bfloat16, max_sessions=4)
+    conv = t.subsample_conv_projection.layer1.conv
+    old = conv.stride
+    conv.stride = (1, 1)
+    try:
+        with pytest.raises(ValueError, match="stride 2"):
+            StreamingConformerAudioTower(t, e, device="cuda", dtype=torch.bfloat16, max_sessions=4)
+    finally:
+        conv.stride = old
+    t.train()
+    try:
+        with pytest.raises(ValueError, match="eval mode"):
+            StreamingConformerAudioTower(t, e, device="cuda", dtype=torch.bfloat16, max_sessions=4)
+    finally:
+        t.eval()
+
+
+def test_session_churn_recycles_handles_and_matches_oracle(modules, pkg):
+    """More than 10x max_handles distinct sessions through one tower: sessions
+    join and leave every tick (leaving = close_session -> reset), abort and
+    rollback release the handles they introduced, and every tick's raw tokens
+    match the oracle."""
+    from gemma4_omni_b200.config import SMALL
+    from gemma4_omni_b200.weights import bf16_round
+    from helpers import oracle_config
+
+    st = tower(modules, 8)
+    max_handles = st._engine.max_handles
+    _, _, w = modules
+    model = conformer_ref.OracleConformer({k: torch.from_numpy(bf16_round(np.asarray(v))) for k, v in w.items()},
+                                          oracle_config(SMALL))
+    zero = {k: v[0] for k, v in conformer_ref.zero_state(model.cfg, 1).items()}
+    rng = np.random.default_rng(99)
+    g = torch.Generator().manual_seed(98)
+    live: dict[str, int] = {}  # session -> next frame
+    states: dict[str, dict] = {}
+    next_id = 0
+    total = 0
+    tick = 0
+    while next_id < 10 * max_handles + 40:
+        for sid in [s for s in live if rng.random() < 0.25]:  # leavers
+            st.reset(sid)
+            live.pop(sid)
+            states.pop(sid, None)
+        while len(live) < 8 and rng.random() < 0.9:  # joiners
+            live[f"churn-{next_id}"] = 0
+            next_id += 1
+        if not live:
+            continue
+        sids = list(live)
+        rng.shuffle(sids)
+        n = len(sids)
+        mel = torch.randn((n, 8, 128), generator=g)
+        p = st.prepare_batch(mel.cuda(), tuple(cursor(s, live[s]) for s in sids))
+        action = rng.random()
+        if action < 0.08:
+            p.abort()
+            continue
+        raw = p.raw_tokens.float().cpu()
+        p.commit()
+        if action < 0.12:
+            p.rollback_committed()
+            continue
+        state = {k: torch.stack([states.get(s, zero)[k] for s in sids]) for k in zero}
+        reset = torch.tensor([s not in states for s in sids])
+        ref, _, _, _, nxt = model.step(mel, torch.ones(n, 8, dtype=torch.bool), state, reset)
+        assert_parity(raw, ref, f"churn tick {tick}")
+        for i, s in enumerate(sids):
+            states[s] = {k: v[i] for k, v in nxt.items()}
+            live[s] += 1
+        total += n
+        tick += 1
+    assert next_id > 10 * max_handles and len(st._handles) <= 8
+    assert len(st._free_handles) + len(st._handles) == max_handles
+    assert st._engine.status() == 0
+    st.close()
+
+
+def test_pcm_entry_matches_cpu_mel_through_prepare_batch(modules):
+    """prepare_batch_pcm (GPU log-mel with the tail in the slot) equals
+    prepare_batch on the reference extractor's mel, across ticks, a reset and
+    a session that joins late."""
+    from gemma4_omni_b200 import synthetic
+    from oracle import mel_ref
+
+    a, b = tower(modules, 4), tower(modules, 4)
+    tails = {}
+    plan = [["p", "q"], ["p", "q"], ["q", "p", "r"], ["p", "r"], ["q", "r", "p"]]
+    frames = {"p": 0, "q": 0, "r": 0}
+    for t, sids in enumerate(plan):
+        if t == 3:  # q leaves and comes back later with a fresh state
+            a.reset("q")
+            b.reset("q")
+            frames["q"] = 0
+            tails.pop("q", None)
+        pcm = np.stack([synthetic.session_audio(5, {"p": 1, "q": 2, "r": 3}[s], 1, first_frame=frames[s], total_frames=8)[0]
+                        for s in sids])
+        mels = []
+        for i, s in enumerate(sids):
+            m, tails[s] = mel_ref.extract_single_frame(pcm[i], tails.get(s))
+            mels.append(m)
+        cur = tuple(cursor(s, frames[s]) for s in sids)
+        pa = a.prepare_batch_pcm(torch.from_numpy(pcm).cuda(), cur)
+        pb = b.prepare_batch(torch.from_numpy(np.stack(mels)).cuda(), cur)
+        assert pa.reset_reasons == pb.reset_reasons
+        assert_parity(pa.soft_tokens, pb.soft_tokens.float(), f"pcm vs mel tick {t}", 0.9999, 1e-2)
+        pa.commit()
+        pb.commit()
+        for s in sids:
+            frames[s] += 1
+    a.close()
+    b.close()
+
+
+def _listener_batch(manifest_id, rows, pcm):
+    """Stand-ins with the attribute layout of the reference's ListenerBatch /
+    BatchRowDescriptor / ListenerFrame / ListenerSessionState
+    (duplex_kernel/microbatch_contract.py)."""
+    from types import SimpleNamespace as NS
+    descs = tuple(NS(session_id=s, session_generation=g, state_epoch_id=e, frame_id=f, sequence_position=f)
+                  for s, g, e, f in rows)
+    frames = tuple(NS(session_id=s, frame_id=f, pcm=pcm[i]) for i, (s, _, _, f) in enumerate(rows))
+    manifest = NS(manifest_id=manifest_id, batch_size=len(rows), rows=descs)
+    states = tuple(NS(session_id=s) for s, _, _, _ in rows)
+    return NS(manifest=manifest, frames=frames), states
+
+
+def test_frontend_encode_batch_matches_reference_pcm_golden(pkg):
+    """ListenerMicrobatchAudioFrontend.encode_batch from PCM (GPU mel) against
+    the reference's PCM -> _extract_single_frame -> streaming tower run
+    (tests/golden/pcm_tower_nt.npz), at the parity gate."""
+    import json
+    from pathlib import Path
+
+    from gemma4_omni_b200.config import SMALL
+    from gemma4_omni_b200.listener_frontend import ListenerMicrobatchAudioFrontend
+    from gemma4_omni_b200.streaming_conformer import StreamingConformerAudioTower
+
+    g = np.load(Path(__file__).resolve().parent / "golden" / "pcm_tower_nt.npz")
+    t, e, _ = hf_modules(SMALL, int(g["seed_w"]))
+    st = StreamingConformerAudioTower(t, e, device="cuda", dtype=torch.bfloat16, max_sessions=4)
+    fe = ListenerMicrobatchAudioFrontend(None, None, device="cuda", dtype=torch.bfloat16, streaming_audio_tower=st)
+    off = 0
+    for k, rows in enumerate(json.loads(str(g["rows"]))):
+        n = len(rows)
+        batch, states = _listener_batch(f"m{k}", rows, g["pcm"][off:off + n])
+        prepared = fe.encode_batch(batch, states)
+        assert prepared.streaming_audio_input_shape == (n, 8, 128)
+        assert [c.session_id for c in prepared.audio_stream_cursors] == [r[0] for r in rows]
+        soft = torch.stack(prepared.audio_soft_tokens)
+        assert soft.dtype == torch.bfloat16 and tuple(soft.shape) == (n, 2, SMALL.text_hidden)
+        assert_parity(soft, torch.from_numpy(g["soft"][off:off + n]), f"soft tick {k}")
+        assert_parity(torch.stack(prepared.audio_tower_raw_tokens), torch.from_numpy(g["raw"][off:off + n]),
+                      f"raw tick {k}")
+        prepared.commit()
+        torch.cuda.synchronize()
+        copy_ms, _, tower_ms = prepared.cuda_phase_timings_after_completion()
+        assert copy_ms is not None and tower_ms is not None and tower_ms > 0
+        off += n
+    fe.close()
+
+
+def test_frontend_transaction_rules(modules):
+    """One active manifest, single owner thread, poisoning after an abort."""
+    import threading
+
+    from gemma4_omni_b200.listener_frontend import ListenerMicrobatchAudioFrontend
+
+    fe = ListenerMicrobatchAudioFrontend(None, None, device="cuda", dtype=torch.bfloat16,
+                                         streaming_audio_tower=tower(modules, 4))
+    pcm = np.zeros((2, 1280), np.float32)
+    batch, states = _listener_batch("a", [("x", 0, "e", 0), ("y", 0, "e", 0)], pcm)
+    p = fe.encode_batch(batch, states)
+    with pytest.raises(RuntimeError, match="has not committed"):
+        fe.encode_batch(*_listener_batch("b", [("x", 0, "e", 1)], pcm[:1]))
+    with pytest.raises(RuntimeError, match="while a batch is prepared"):
+        fe.close_session("x")
+    errors = []
+
+    def commit_elsewhere():
+        try:
+            p.commit()
+            errors.append("committed from another thread")
+        except RuntimeError as exc:
+            errors.append(str(exc))
+
+    th = threading.Thread(target=commit_elsewhere)
+    th.start()
+    th.join()
+    assert errors and "single owner thread" in errors[0], errors
+    p.commit()
+    fe.close_session("x")
+    p2 = fe.encode_batch(*_listener_batch("c", [("y", 0, "e", 1)], pcm[:1]))
+    p2.abort()
+    with pytest.raises(RuntimeError, match="poisoned"):
+        fe.encode_batch(*_listener_batch("d", [("y", 0, "e", 1)], pcm[:1]))
+    fe.close()

@@ -55,11 +55,30 @@ def committed(eng, book):
 
 
 def test_packer_replays_reference_slot_trace(small_weights):
+    """Also checks lb_get_counters against the trace: calls, rows per reason,
+    committed rows and the status history of the exhausted-bank steps."""
     g = np.load(GOLD / "packer.npz")
     S = int(g["max_sessions"])
     eng = engine(small_weights, S, 16, rows=S)
     book = HandleBook()
+    want = {"packs": 0, "steps": 0, "commits": 0, "aborts": 0, "resets": 0, "rows_stepped": 0,
+            "rows_committed": 0}
+    reasons_seen = dict.fromkeys(REASONS, 0)
     for ev in json.loads(str(g["events"])):
+        if ev["kind"] in ("reset", "reset_session"):
+            want["resets"] += int(ev["kind"] == "reset_session" or ev["sid"] in book.handles)
+        elif "error" in ev:
+            want.update(packs=want["packs"] + 1, steps=want["steps"] + 1, aborts=want["aborts"] + 1,
+                        rows_stepped=want["rows_stepped"] + len(ev["rows"]))
+        else:
+            n = len(ev["rows"])
+            want.update(packs=want["packs"] + 1, steps=want["steps"] + 1, rows_stepped=want["rows_stepped"] + n)
+            for r in ev["reasons"]:
+                reasons_seen[r] += 1
+            if ev["action"] == "commit":
+                want.update(commits=want["commits"] + 1, rows_committed=want["rows_committed"] + n)
+            else:
+                want["aborts"] += 1
         if ev["kind"] == "reset":
             if ev["sid"] in book.handles:
                 eng.reset_handle(book.handle(ev["sid"]))
@@ -80,6 +99,16 @@ def test_packer_replays_reference_slot_trace(small_weights):
             eng.commit() if ev["action"] == "commit" else eng.abort()
         assert committed(eng, book) == sorted(tuple(x) for x in ev["committed"])
     assert eng.status() == 0
+    ctr = eng.counters()
+    for k, v in want.items():
+        assert ctr[k] == v, (k, ctr[k], v)
+    # rows of the exhausted-bank packs are counted by reason too (they resolved)
+    assert ctr["rows_continue"] >= reasons_seen["continue"]
+    assert ctr["rows_identity_reset"] >= reasons_seen["identity_reset"]
+    assert ctr["rows_gap_or_cursor_mismatch"] >= reasons_seen["gap_or_cursor_mismatch"]
+    assert sum(ctr[f"rows_{r}"] for r in REASONS) == want["rows_stepped"]
+    assert ctr["stale_commits"] == 0 and ctr["status"] == 0
+    assert ctr["status_history"] & 2  # the exhausted-bank steps' LB_DEV_SLOT_EXHAUSTED
     eng.close()
 
 
@@ -187,3 +216,30 @@ def test_state_machine_rejects_out_of_order_calls(small_weights):
         eng.reset_handle(0)  # not while a batch is prepared
     eng.abort()
     eng.close()
+
+
+def test_reset_handles_releases_many_at_once(small_weights):
+    """lb_reset_handles_async == one lb_reset_handle_async per handle."""
+    eng = engine(small_weights, 8, 16, rows=8)
+    ref = engine(small_weights, 8, 16, rows=8)
+    book = HandleBook()
+    rows = [(f"s{i}", 0, "e", 0) for i in range(6)]
+    for e in (eng, ref):
+        step_rows(e, book, rows)
+        e.commit()
+    gone = [1, 4, 5]
+    eng.reset_handles(torch.tensor([book.handle(f"s{i}") for i in gone], dtype=torch.int32, device="cuda"))
+    for i in gone:
+        ref.reset_handle(book.handle(f"s{i}"))
+    assert all((a == b).all() for a, b in zip(eng.read_handles(), ref.read_handles()))
+    nxt = [(f"s{i}", 0, "e", 1) for i in (0, 2, 3)] + [("t0", 0, "e", 0), ("t1", 0, "e", 0)]
+    got = step_rows(eng, book, nxt)
+    want = step_rows(ref, book, nxt)
+    assert list(got[0]) == list(want[0]) and list(got[1]) == list(want[1])
+    assert sorted(got[0][3:]) == [1, 4]  # the lowest freed slots
+    bad = torch.tensor([99], dtype=torch.int32, device="cuda")
+    eng.abort()
+    eng.reset_handles(bad)
+    assert eng.status() & 8  # LB_DEV_BAD_HANDLE
+    eng.close()
+    ref.close()

@@ -95,6 +95,42 @@ def test_rejects_sizes_beyond_scratch(lib):
     assert rc == LB_ERR_CAPACITY
 
 
+def test_rejects_bad_shapes_strides_and_alignment(lib):
+    stream = torch.cuda.current_stream().cuda_stream
+    x = torch.zeros(8, 512, dtype=torch.bfloat16, device="cuda")
+    w = torch.zeros(512, 512, dtype=torch.bfloat16, device="cuda")
+    out = torch.zeros(8, 512, dtype=torch.bfloat16, device="cuda")
+
+    def call(xp=None, x_ld=512, o=256, k=256, outp=None, ld_out=256):
+        return lib.lb_op_gemm_splitk_scratch(xp or x.data_ptr(), x_ld, 8, w.data_ptr(), 0, None, None, o, k,
+                                             outp or out.data_ptr(), ld_out, 0, 2, None, stream)
+
+    assert call(o=192, ld_out=192) == -1                # out_features not a multiple of 128
+    assert call(k=96) == -1                             # k not a multiple of 64
+    assert call(ld_out=128) == -1                       # ld_out < out_features
+    assert call(outp=out.data_ptr() + 2) == -1          # out not 16-byte aligned
+    assert call(x_ld=128) == -1                         # x_ld < k: rows would overlap
+    assert call(xp=x.data_ptr() + 2) == -1              # x not 16-byte aligned
+    assert call() == 0
+    torch.cuda.synchronize()
+
+
+def test_splits_beyond_k_blocks_are_clamped(lib):
+    """splits > k/64 runs with one K block per split; the result still matches lb_op_gemm."""
+    stream = torch.cuda.current_stream().cuda_stream
+    m, o, k = 40, 1536, 512  # 8 K blocks
+    x, w, _, b = _operands(m, o, k, 0, True, seed=77)
+    ref = torch.zeros(m, o, dtype=torch.bfloat16, device="cuda")
+    assert lib.lb_op_gemm(x.data_ptr(), k, m, w.data_ptr(), 0, None, b.data_ptr(), o, k, ref.data_ptr(), o, 0, 0,
+                          1, None, stream) == 0
+    out = torch.zeros(m, o, dtype=torch.bfloat16, device="cuda")
+    assert lib.lb_op_gemm_splitk_scratch(x.data_ptr(), k, m, w.data_ptr(), 0, None, b.data_ptr(), o, k,
+                                         out.data_ptr(), o, 0, 64, None, stream) == 0
+    torch.cuda.synchronize()
+    ref = ref.float()
+    assert bool(((out.float() - ref).abs() <= 1.6e-2 * ref.abs() + 4e-3 * ref.abs().max()).all())
+
+
 def test_fresh_process():
     res = subprocess.run([sys.executable, str(Path(__file__).resolve())], capture_output=True,
                          text=True, timeout=600)
