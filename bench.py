@@ -70,6 +70,7 @@ def parse():
     ap.add_argument("--weights", default="int8", choices=["int8", "bf16"])
     ap.add_argument("--no-sweep", action="store_true", help="skip the real-time capacity sweep")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-small", action="store_true", help="skip the small-N weight-streaming sweep")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--cpu-sessions", type=int, default=256,
                     help="sessions of the CPU port's bounded sample of the workload")
@@ -317,7 +318,7 @@ def run_ours(args, pkg, rank, world, device):
     one_gpu = world == 1
     sweep = [] if (args.no_sweep or not one_gpu) else [256, 1024, 2048, 4096, 8192]
     c4_n = args.c4_sessions // world if args.c4_steps > 0 else 0
-    cap = max([n, c4_n] + sweep)
+    cap = max([n, c4_n, 16] + sweep)
     eng = runtime.ListenerEngine(FULL, max_sessions=cap, max_rows=cap, max_handles=cap, weight_format=fmt,
                                  device=device)
     tower, film = synth_weights(pkg)
@@ -433,7 +434,7 @@ def run_ours(args, pkg, rank, world, device):
     # ---- weight-streaming regime: small N, device-resident, step time vs the
     # step's algorithmic bytes (weights + per-session state)
     small = {}
-    if one_gpu:
+    if one_gpu and not args.no_small:
         for ns in (1, 4, 16, 64):
             sc = Schedule(pkg, ns, 230, seed=300 + ns).device(device)
             pc = dev_pcm[:, :ns].contiguous()
