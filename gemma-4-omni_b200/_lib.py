@@ -99,9 +99,11 @@ SIGNATURES: dict[str, tuple] = {
     "lb_step_kernel_count": (I, [P]),
     "lb_debug_read_buffer": (I, [P, ctypes.c_char_p, P, ctypes.c_size_t, P]),
     "lb_get_counters": (I, [P, ctypes.POINTER(LbCounters), P]),
+    "lb_mel_async": (I, [P, I, P, P, P, P, P]),
+    "lb_film_talker_async": (I, [P, I, P, I, P, P, P, P, P]),
     "lb_reset_handles_async": (I, [P, I, P, P]),
     "lb_op_gemm": (I, [P, I, I, P, I, P, P, I, I, P, I, I, I, I, P, P]),
-    "lb_op_gemm_clipped": (I, [P, I, I, I, P, I, P, P, I, I, P, I, I, I, I, I, P, P, P, P]),
+    "lb_op_gemm_clipped": (I, [P, I, I, I, P, I, P, P, I, I, P, I, I, I, I, I, P, P, P, P, P]),
     "lb_op_gemm_splitk_scratch": (I, [P, I, I, P, I, P, P, I, I, P, I, I, I, P, P]),
     "lb_snapshot_ready_rows": (I, [I, P, P, P, P, P, P, P, I64, P, P, P, P, P]),
     "lb_order_ready_heads": (I, [I, P, P, P, I64, I64, I, P, P, P, P]),

@@ -38,12 +38,15 @@ extern "C" {
 int lb_op_gemm_clipped(const void* x, int x_ld, int m, int x_part_rows, const void* w, int w_int8,
                        const void* w_scale, const float* bias, int out_features, int k, void* out,
                        int ld_out, int out_mode, int act, int splits, int parts,
-                       const float* out_bounds, const float* post_bounds, int* status_dev,
-                       void* stream) {
+                       const float* out_bounds, const float* post_bounds, float* split_acc,
+                       int* status_dev, void* stream) {
   if (!x || !w || !out || m <= 0 || out_features <= 0 || k <= 0) return LB_ERR_INVALID_ARGUMENT;
   if (w_int8 < 0 || w_int8 > 2 || (w_int8 && !w_scale)) return LB_ERR_INVALID_ARGUMENT;
   if (out_mode < 0 || out_mode > 2 || act < 0 || act > 1 || splits < 1) return LB_ERR_INVALID_ARGUMENT;
-  if (splits > 1 && out_mode != 2) return LB_ERR_INVALID_ARGUMENT;
+  // a split-K bf16 / fp32 output reduces through the caller's zeroed fp32
+  // workspace and a finish pass (which leaves it zeroed)
+  const bool split_ws = splits > 1 && out_mode != 2;
+  if (split_ws && !split_acc) return LB_ERR_INVALID_ARGUMENT;
   // the activation and weight maps start on 16-byte boundaries and rows do not overlap
   if (x_ld < k || !aligned16(x) || !aligned16(w) || ld_out < out_features) return LB_ERR_INVALID_ARGUMENT;
   if (parts < 1 || parts > GemmParams::kMaxParts || out_features % (128 * parts) != 0 || x_part_rows < 0 ||
@@ -66,37 +69,53 @@ int lb_op_gemm_clipped(const void* x, int x_ld, int m, int x_part_rows, const vo
     // the next-input clamp follows the activation of a bf16 output only
     if (out_mode != 0 && (std::isfinite(p.post_lo) || std::isfinite(p.post_hi))) return LB_ERR_INVALID_ARGUMENT;
   }
-  // split-K partial sums cannot be clamped before they are summed
+  // atomically accumulated partial sums cannot be clamped before they are summed
   if (out_mode == 2 && finite) return LB_ERR_INVALID_ARGUMENT;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return LB_ERR_CUDA;
   if (dev < 0 || dev >= kMaxDevices) return LB_ERR_INVALID_ARGUMENT;
   if (ensure_gemm_attributes(dev) != cudaSuccess) return LB_ERR_CUDA;
   GemmPlan plan;
-  int rc = gemm_prepare(&plan, w, w_int8, out_features, k, x, x_ld, m, out, ld_out, out_mode, false,
+  int rc = gemm_prepare(&plan, w, w_int8, out_features, k, x, x_ld, m, split_ws ? split_acc : out,
+                        split_ws ? out_features : ld_out, split_ws ? 2 : out_mode, false,
                         x_part_rows > 0 ? parts : 1, x_part_rows);
   if (rc) return rc == -3 ? LB_ERR_INVALID_ARGUMENT : LB_ERR_CUDA;
   p.m_static = m;
   p.w_scale = static_cast<const __half*>(w_scale);
   p.bias = bias;
-  p.out = out;
-  p.ld_out = ld_out;
-  p.out_mode = out_mode;
+  p.out = split_ws ? static_cast<void*>(split_acc) : out;
+  p.ld_out = split_ws ? out_features : ld_out;
+  p.out_mode = split_ws ? 2 : out_mode;
   p.act = act;
   p.status = status_dev;
   if (parts > 1) {
     p.part_o = out_features / parts;
     p.x_part_rows = x_part_rows;
   }
-  cudaError_t e = gemm_launch(plan, p, splits, static_cast<cudaStream_t>(stream));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = gemm_launch(plan, p, splits, s);
+  if (e == cudaSuccess && split_ws) {
+    FinalizeClip fc;
+    fc.part_o = p.part_o;
+    for (int j = 0; j < 3; ++j) {
+      fc.lo[j] = parts > 1 ? p.part_lo[j] : p.out_lo;
+      fc.hi[j] = parts > 1 ? p.part_hi[j] : p.out_hi;
+    }
+    fc.plo = p.post_lo;
+    fc.phi = p.post_hi;
+    e = launch_split_finish(nullptr, m, m, split_acc, out_features, act, out, ld_out, out_mode == 1, false, fc,
+                            false, s);
+  }
   return e == cudaSuccess ? LB_OK : LB_ERR_CUDA;
 }
 
 int lb_op_gemm(const void* x, int x_ld, int m, const void* w, int w_int8, const void* w_scale,
                const float* bias, int out_features, int k, void* out, int ld_out, int out_mode,
                int act, int splits, int* status_dev, void* stream) {
+  if (splits > 1 && out_mode != 2) return LB_ERR_INVALID_ARGUMENT;
   return lb_op_gemm_clipped(x, x_ld, m, 0, w, w_int8, w_scale, bias, out_features, k, out, ld_out,
-                            out_mode, act, splits < 1 ? 1 : splits, 1, nullptr, nullptr, status_dev, stream);
+                            out_mode, act, splits < 1 ? 1 : splits, 1, nullptr, nullptr, nullptr, status_dev,
+                            stream);
 }
 
 }  // extern "C"

@@ -386,6 +386,7 @@ size_t layout_acts(Ctx& c, char* base) {
   if (base) {
     c.in_pcm = pcm; c.in_mel = mel; c.in_query = qry; c.sub_in = sub; c.h = h; c.y = y; c.xa = xa;
     c.xf = xf; c.qkv = qkv; c.att = att; c.gl = gl; c.wide_acc = wa; c.out_raw = oraw;
+    c.wide_width = static_cast<int>(wide);
     c.out_soft = osoft; c.out_film = ofilm; c.film_xq = fxq; c.film_xr = fxr; c.film_qd = fqd;
     c.film_rd_bf = frb; c.film_gb = fgb; c.film_fused = ffu; c.film_map = fmap; c.film_amp = famp;
     c.xe = xe;
@@ -421,6 +422,7 @@ int make_op(Ctx& c, GemmOp& op, void* w, const __half* scale, int O, int K, cons
     scale = nullptr;
   }
   if (out_kind == 2) out_kind = 0;
+  op.pdl = c.pdl;
   GemmParams& p = op.params;
   p = GemmParams();
   p.m_dev = c.dev_counts + 1;
@@ -451,17 +453,21 @@ int make_op(Ctx& c, GemmOp& op, void* w, const __half* scale, int O, int K, cons
       p.x_part_rows = 2 * c.cfg.max_rows;
     }
   }
-  op.splits = finite_out && out_kind == 1 ? 1 : gemm_pick_splits(O, K, tok_cap, c.num_sms);
-  if (out_kind == 0) {
-    // A split bf16 output goes through an fp32 partial-sum buffer and a finalize
-    // pass; worth it only while the tiles cannot fill half of the SMs.
-    const int tn = gemm_token_tile(O, tok_cap, c.num_sms);
-    const int tiles = (O / 128) * ((tok_cap + tn - 1) / tn);
-    if (tiles * 2 >= c.num_sms) op.splits = 1;
-  }
+  (void)finite_out;  // the finish pass of a split-K op clamps
+  op.splits = gemm_pick_splits(O, K, tok_cap, c.num_sms);
+  const int tn = gemm_token_tile(O, tok_cap, c.num_sms);
+  const int tiles = (O / 128) * ((tok_cap + tn - 1) / tn);
+  // A split output goes through the fp32 partial-sum buffer and one finish
+  // pass; worth it only while the tiles cannot fill half of the SMs.
+  if (tiles * 2 >= c.num_sms || O > c.wide_width) op.splits = 1;
+  op.out_kind = out_kind;
+  op.out = out;
   if (op.splits > 1) {
+    // K slices reduce-add into the context's partial-sum buffer (kept zero:
+    // every finish pass zeroes what it read), then the finish pass (run_op)
     p.out_mode = 2;
-    p.out = out_kind == 0 ? static_cast<void*>(c.wide_acc) : out;
+    p.out = c.wide_acc;
+    p.ld_out = O;
   } else {
     p.out_mode = out_kind == 0 ? 0 : 1;
     p.out = out;
@@ -470,28 +476,22 @@ int make_op(Ctx& c, GemmOp& op, void* w, const __half* scale, int O, int K, cons
                       op.final_f16, x_parts, p.x_part_rows);
 }
 
-cudaError_t run_op(Ctx& c, const GemmOp& op, int tok_cap, __nv_bfloat16* final_bf16, cudaStream_t s) {
-  if (op.splits > 1) {
-    cudaError_t e = cudaMemsetAsync(op.params.out, 0,
-                                    static_cast<size_t>(tok_cap) * op.plan.O * sizeof(float), s);
-    if (e != cudaSuccess) return e;
+// One GEMM launch, plus the finish pass of a split-K op (clamps, SiLU, the
+// output store and the re-zeroing of the partial-sum buffer).  No memset: the
+// partial-sum buffer is zero at creation and after every finish pass.
+cudaError_t run_op(Ctx& c, const GemmOp& op, int tok_cap, cudaStream_t s) {
+  cudaError_t e = gemm_launch(op.plan, op.params, op.splits, s, op.pdl);
+  if (e != cudaSuccess || op.splits <= 1) return e;
+  FinalizeClip fc;
+  fc.part_o = op.params.part_o;
+  for (int j = 0; j < 3; ++j) {
+    fc.lo[j] = fc.part_o ? op.params.part_lo[j] : op.params.out_lo;
+    fc.hi[j] = fc.part_o ? op.params.part_hi[j] : op.params.out_hi;
   }
-  cudaError_t e = gemm_launch(op.plan, op.params, op.splits, s);
-  if (e != cudaSuccess) return e;
-  if (op.splits > 1 && final_bf16) {
-    // finalize: output clamp -> activation -> next linear's input clamp -> bf16
-    FinalizeClip fc;
-    fc.part_o = op.params.part_o;
-    for (int j = 0; j < 3; ++j) {
-      fc.lo[j] = fc.part_o ? op.params.part_lo[j] : op.params.out_lo;
-      fc.hi[j] = fc.part_o ? op.params.part_hi[j] : op.params.out_hi;
-    }
-    fc.plo = op.params.post_lo;
-    fc.phi = op.params.post_hi;
-    e = launch_finalize_wide(c, tok_cap, static_cast<const float*>(op.params.out), op.plan.O,
-                             op.params.act, final_bf16, fc, op.final_f16, s);
-  }
-  return e;
+  fc.plo = op.params.post_lo;
+  fc.phi = op.params.post_hi;
+  return launch_split_finish(c.dev_counts + 1, 0, tok_cap, c.wide_acc, op.plan.O, op.params.act, op.out,
+                             op.plan.O, op.out_kind == 1, op.final_f16, fc, c.pdl_all, s);
 }
 
 int build_plans(lb_ctx* x, int bi) {
@@ -557,7 +557,7 @@ cudaError_t run_tower(lb_ctx* x, int bi, int input_kind, cudaStream_t s) {
   const int tc = b.tok_cap, rc = b.rows_cap, d = g.hidden;
   LB_TRY(launch_mel(c, rc, input_kind, s));
   LB_TRY(launch_subsample(c, rc, s));
-  LB_TRY(run_op(c, P.in_proj, tc, nullptr, s));
+  LB_TRY(run_op(c, P.in_proj, tc, s));
   {
     RowFusedArgs r;
     r.pre_w = c.w.layers[0].ffn_pre[0];
@@ -572,9 +572,9 @@ cudaError_t run_tower(lb_ctx* x, int bi, int input_kind, cudaStream_t s) {
     LayerW& L = c.w.layers[i];
     lb_ctx::LayerOps& o = P.layers[i];
     // FFN1
-    LB_TRY(run_op(c, o.ffn1[0], tc, c.xf, s));
+    LB_TRY(run_op(c, o.ffn1[0], tc, s));
     LB_STOP(i, 0);
-    LB_TRY(run_op(c, o.ffn1[1], tc, nullptr, s));
+    LB_TRY(run_op(c, o.ffn1[1], tc, s));
     LB_STOP(i, 1);
     {
       RowFusedArgs r;
@@ -596,11 +596,11 @@ cudaError_t run_tower(lb_ctx* x, int bi, int input_kind, cudaStream_t s) {
     }
     LB_STOP(i, 2);
     // attention
-    LB_TRY(run_op(c, o.qkv, tc, c.qkv, s));
+    LB_TRY(run_op(c, o.qkv, tc, s));
     LB_STOP(i, 3);
     LB_TRY(launch_attention(c, i, rc, s));
     LB_STOP(i, 4);
-    LB_TRY(run_op(c, o.post, tc, nullptr, s));
+    LB_TRY(run_op(c, o.post, tc, s));
     LB_STOP(i, 5);
     {
       RowFusedArgs r;
@@ -615,11 +615,11 @@ cudaError_t run_tower(lb_ctx* x, int bi, int input_kind, cudaStream_t s) {
     }
     LB_STOP(i, 6);
     // light conv
-    LB_TRY(run_op(c, o.lstart, tc, c.gl, s));
+    LB_TRY(run_op(c, o.lstart, tc, s));
     LB_STOP(i, 7);
     LB_TRY(launch_lconv(c, i, rc, s));
     LB_STOP(i, 8);
-    LB_TRY(run_op(c, o.lend, tc, nullptr, s));
+    LB_TRY(run_op(c, o.lend, tc, s));
     LB_STOP(i, 9);
     {
       RowFusedArgs r;
@@ -632,9 +632,9 @@ cudaError_t run_tower(lb_ctx* x, int bi, int input_kind, cudaStream_t s) {
     }
     LB_STOP(i, 10);
     // FFN2 + norm_out (+ next layer's FFN1 pre-norm, or plain bf16 for output_proj)
-    LB_TRY(run_op(c, o.ffn2[0], tc, c.xf, s));
+    LB_TRY(run_op(c, o.ffn2[0], tc, s));
     LB_STOP(i, 11);
-    LB_TRY(run_op(c, o.ffn2[1], tc, nullptr, s));
+    LB_TRY(run_op(c, o.ffn2[1], tc, s));
     LB_STOP(i, 12);
     {
       RowFusedArgs r;
@@ -655,9 +655,9 @@ cudaError_t run_tower(lb_ctx* x, int bi, int input_kind, cudaStream_t s) {
       LB_TRY(launch_row_fused(c, tc, r, s));
     }
   }
-  LB_TRY(run_op(c, P.out_proj, tc, nullptr, s));
+  LB_TRY(run_op(c, P.out_proj, tc, s));
   LB_TRY(launch_outputs(c, tc, 0, s));
-  LB_TRY(run_op(c, P.embed, tc, nullptr, s));
+  LB_TRY(run_op(c, P.embed, tc, s));
   LB_TRY(launch_outputs(c, tc, 1, s));
   return cudaSuccess;
 }
@@ -668,11 +668,11 @@ cudaError_t run_film(lb_ctx* x, int bi, cudaStream_t s) {
   lb_ctx::Plans& P = x->plans[bi];
   const int tc = c.buckets[bi].tok_cap;
   LB_TRY(launch_film(c, tc, 0, s));
-  LB_TRY(run_op(c, P.qdown, tc, nullptr, s));
-  LB_TRY(run_op(c, P.rdown, tc, c.film_rd_bf, s));
-  LB_TRY(run_op(c, P.film, tc, nullptr, s));
+  LB_TRY(run_op(c, P.qdown, tc, s));
+  LB_TRY(run_op(c, P.rdown, tc, s));
+  LB_TRY(run_op(c, P.film, tc, s));
   LB_TRY(launch_film(c, tc, 1, s));
-  LB_TRY(run_op(c, P.fout, tc, nullptr, s));
+  LB_TRY(run_op(c, P.fout, tc, s));
   LB_TRY(launch_film(c, tc, 2, s));
   return cudaSuccess;
 }
@@ -730,6 +730,12 @@ int lb_create(const lb_config* cfg, lb_ctx** out_ctx) {
   c.cfg = *cfg;
   c.hd = cfg->hidden / cfg->heads;
   c.weight_int8 = cfg->weight_format == LB_WEIGHTS_INT8;
+  {
+    const char* pdl_env = std::getenv("LB_PDL");
+    const int mode = pdl_env ? std::atoi(pdl_env) : 1;
+    c.pdl = mode >= 1;
+    c.pdl_all = mode >= 2;
+  }
   c.max_handles = cfg->max_handles;
   if (cudaGetDevice(&c.device) != cudaSuccess) return LB_ERR_CUDA;
   cudaDeviceGetAttribute(&c.num_sms, cudaDevAttrMultiProcessorCount, c.device);
@@ -1178,6 +1184,56 @@ int lb_clear_status(lb_ctx* x, void* stream) {
   if (!x) return LB_ERR_INVALID_ARGUMENT;
   cudaSetDevice(x->c.device);
   return err_of(launch_clear_status(x->c, static_cast<cudaStream_t>(stream)));
+}
+
+int lb_mel_async(lb_ctx* x, int n, const float* pcm, const float* tail_in, float* tail_out, float* mel_out,
+                 void* stream) {
+  if (!x || n < 0 || (n > 0 && (!pcm || !tail_out || !mel_out))) return LB_ERR_INVALID_ARGUMENT;
+  if (tail_in && tail_in == tail_out) return LB_ERR_INVALID_ARGUMENT;
+  Ctx& c = x->c;
+  if (!c.weights_final) return LB_ERR_STATE;  // the window and filterbank are weights
+  if (n == 0) return LB_OK;
+  cudaSetDevice(c.device);
+  return err_of(launch_mel_standalone(c, n, pcm, tail_in, tail_out, mel_out, static_cast<cudaStream_t>(stream)));
+}
+
+int lb_film_talker_async(lb_ctx* x, int n, const void* response_hidden, int max_states, const int32_t* n_states,
+                         const int32_t* steps, const void* query, void* out, void* stream) {
+  if (!x || n < 0 || max_states < 1) return LB_ERR_INVALID_ARGUMENT;
+  if (n > 0 && (!response_hidden || !n_states || !steps || !query || !out)) return LB_ERR_INVALID_ARGUMENT;
+  Ctx& c = x->c;
+  if (!c.cfg.film_enabled) return LB_ERR_INVALID_ARGUMENT;
+  if (!c.weights_final) return LB_ERR_STATE;
+  if (c.state == 1 || c.state == 2) return LB_ERR_STATE;  // the FiLM buffers belong to a packed step
+  if (n == 0) return LB_OK;
+  // FiLM runs over "tokens": one per talker row; the bucket holding n tokens
+  int bi = -1;
+  for (size_t i = 0; i < c.buckets.size(); ++i)
+    if (c.buckets[i].tok_cap >= n) {
+      bi = static_cast<int>(i);
+      break;
+    }
+  if (bi < 0) return LB_ERR_CAPACITY;
+  cudaSetDevice(c.device);
+  int rc = build_plans(x, bi);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const auto* hid = static_cast<const __nv_bfloat16*>(response_hidden);
+  const auto* q = static_cast<const __nv_bfloat16*>(query);
+  cudaError_t e = launch_film_talker(c, n, hid, max_states, n_states, steps, q, nullptr, 0, s);
+  if (e == cudaSuccess) {
+    const bool eager = c.dbg_sub || c.dbg_layers || c.dbg_stop_layer >= 0;
+    if (eager) {
+      e = run_film(x, bi, s);
+    } else {
+      rc = ensure_graph(x, bi, 2);
+      if (rc) return rc;
+      e = cudaGraphLaunch(x->plans[bi].graph[2], s);
+    }
+  }
+  if (e == cudaSuccess) e = launch_film_talker(c, n, hid, max_states, n_states, steps, q,
+                                               static_cast<__nv_bfloat16*>(out), 1, s);
+  return err_of(e);
 }
 
 int lb_get_counters(lb_ctx* x, lb_counters* out, void* stream) {

@@ -9,6 +9,7 @@
 #pragma once
 
 #include <cstdint>
+#include <utility>
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -30,6 +31,37 @@ enum StatusBits : int {
   kStatusStaleCommit = 1 << 4,      // commit saw a cursor that changed
   kStatusBadRowCount = 1 << 5,      // device row count outside capacity
 };
+
+// Programmatic dependent launch.  The step's kernels are launched (and
+// captured into the step graph) with programmatic stream serialisation, so a
+// kernel may start while the previous one in the stream is still running.
+// Each kernel executes pdl_wait() -- which returns once the previous kernel
+// has completed and its memory is visible -- before it reads anything that
+// kernel wrote, writes any global memory, or can exit; only reads of
+// read-only data (weights, tables) and on-chip set-up may come before it.
+// Because every kernel waits before it can complete, completion stays ordered
+// down the whole chain.  pdl_trigger() lets the next kernel launch; without
+// the launch attribute both are no-ops.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Launches `kernel` on `stream`, with programmatic stream serialisation when
+// `pdl` is set (host side of the protocol above).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_kernel(bool pdl, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                 cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Upper bound for any single spin-wait: 2 s of wall time on the device clock.
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;

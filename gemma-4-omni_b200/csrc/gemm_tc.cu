@@ -248,6 +248,7 @@ __global__ void __launch_bounds__(GemmCfg<TN, WK>::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_trigger();
 
   if (warp == 0) {
     // ---------------- TMA producer
@@ -256,6 +257,26 @@ __global__ void __launch_bounds__(GemmCfg<TN, WK>::kThreads, 1)
       // int8: the raw weight tile completes on its own barrier, so widening
       // never waits for the activation tile
       const uint32_t tx = WINT8 ? p.b_tx_bytes : kABytes + p.b_tx_bytes;
+      // The weights never depend on the previous kernel in the stream, so the
+      // first ring's worth of weight tiles (the ring starts empty) is requested
+      // before pdl_wait(); the activation tiles, which that kernel produces,
+      // follow it.  In the weight-streaming regime (a few tokens) this overlaps
+      // most of a GEMM's HBM traffic with the kernel before it.
+      int pre = 0;
+      for (int u = blockIdx.x; u < units && pre < S; u += gridDim.x) {
+        const Unit w = unit_of(u, o_tiles, t_tiles, TN, p.kb_per_split, total_kb);
+        for (int i = 0; i < w.nkb && pre < S; ++i, ++pre) {
+          const int k = (w.kb_begin + i) * kBlockK;
+          if (WINT8) {
+            mbar_arrive_expect_tx(&full_w[pre], kRawBytes);
+            tma_load_2d_nohint(stage_raw(pre), &tm_w, &full_w[pre], k, w.o0);
+          } else {
+            mbar_arrive_expect_tx(&full[pre], tx);  // W now, X after the wait
+            tma_load_2d_nohint(stage_a(pre), &tm_w, &full[pre], k, w.o0);
+          }
+        }
+      }
+      pdl_wait();
       int it = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
@@ -265,17 +286,21 @@ __global__ void __launch_bounds__(GemmCfg<TN, WK>::kThreads, 1)
         for (int i = 0; i < w.nkb; ++i, ++it) {
           const int s = it % S;
           const uint32_t ph = (it / S) & 1;
-          if (!mbar_wait(&empty[s], ph ^ 1, p.status)) {
-            ok = false;
-            break;
-          }
           const int k = (w.kb_begin + i) * kBlockK;
-          if (WINT8) {
-            mbar_arrive_expect_tx(&full_w[s], kRawBytes);
-            tma_load_2d_nohint(stage_raw(s), &tm_w, &full_w[s], k, w.o0);
+          if (it >= pre) {
+            if (!mbar_wait(&empty[s], ph ^ 1, p.status)) {
+              ok = false;
+              break;
+            }
+            if (WINT8) {
+              mbar_arrive_expect_tx(&full_w[s], kRawBytes);
+              tma_load_2d_nohint(stage_raw(s), &tm_w, &full_w[s], k, w.o0);
+            }
+            mbar_arrive_expect_tx(&full[s], tx);
+            if (!WINT8) tma_load_2d_nohint(stage_a(s), &tm_w, &full[s], k, w.o0);
+          } else if (WINT8) {
+            mbar_arrive_expect_tx(&full[s], tx);  // the raw W tile is already on its way
           }
-          mbar_arrive_expect_tx(&full[s], tx);
-          if (!WINT8) tma_load_2d_nohint(stage_a(s), &tm_w, &full[s], k, w.o0);
           tma_load_2d(stage_b(s), &tm_x, &full[s], k, x_row, pol_x);
         }
       }
@@ -359,18 +384,18 @@ __global__ void __launch_bounds__(GemmCfg<TN, WK>::kThreads, 1)
           tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * Cfg::kBufCols);
       const size_t ld = static_cast<size_t>(p.ld_out);
       constexpr int NC = Cfg::kCols;
-      auto drain = [&](const uint32_t (&r)[NC], int c) {
+      auto drain = [&](const uint32_t (&r)[NC], int c, float sc, float bi) {
         float y[NC];
         if (clamps) {
           if (silu) {
-            epilogue_math<true, true, NC>(r, y, scale, bias, lo, hi, plo, phi);
+            epilogue_math<true, true, NC>(r, y, sc, bi, lo, hi, plo, phi);
           } else {
-            epilogue_math<false, true, NC>(r, y, scale, bias, lo, hi, plo, phi);
+            epilogue_math<false, true, NC>(r, y, sc, bi, lo, hi, plo, phi);
           }
         } else if (silu) {
-          epilogue_math<true, false, NC>(r, y, scale, bias, lo, hi, plo, phi);
+          epilogue_math<true, false, NC>(r, y, sc, bi, lo, hi, plo, phi);
         } else {
-          epilogue_math<false, false, NC>(r, y, scale, bias, lo, hi, plo, phi);
+          epilogue_math<false, false, NC>(r, y, sc, bi, lo, hi, plo, phi);
         }
         const size_t base = static_cast<size_t>(w.t0 + c) * ld + o;
         const int n = c_end - c;  // >= 1
@@ -404,12 +429,12 @@ __global__ void __launch_bounds__(GemmCfg<TN, WK>::kThreads, 1)
         for (int c = c_begin; c < c_end; c += 2 * NC) {
           const bool more_b = c + NC < c_end;
           if (more_b) tmem_ld_async(tbase + static_cast<uint32_t>(c + NC), rb);
-          drain(ra, c);
+          drain(ra, c, scale, bias);
           if (more_b) {
             tmem_wait_ld(rb);
             const bool more_a = c + 2 * NC < c_end;
             if (more_a) tmem_ld_async(tbase + static_cast<uint32_t>(c + 2 * NC), ra);
-            drain(rb, c + NC);
+            drain(rb, c + NC, scale, bias);
             if (more_a) tmem_wait_ld(ra);
           }
         }
@@ -499,12 +524,12 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 
 template <int TN, int WK>
 cudaError_t launch_gemm_t(const GemmPlan& plan, const GemmParams& p, int splits, int num_sms,
-                          cudaStream_t stream) {
+                          cudaStream_t stream, bool pdl) {
   using Cfg = GemmCfg<TN, WK>;
   const int units = (plan.O / kBlockO) * ((plan.m_cap + TN - 1) / TN) * splits;
   const int grid = units < num_sms ? units : num_sms;
-  gemm_wx_kernel<TN, WK><<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(plan.tm_w, plan.tm_x, p);
-  return cudaGetLastError();
+  return launch_kernel(pdl, gemm_wx_kernel<TN, WK>, dim3(grid), dim3(Cfg::kThreads), Cfg::kSmemBytes, stream,
+                       plan.tm_w, plan.tm_x, p);
 }
 
 template <int TN, int WK>
@@ -680,7 +705,7 @@ int gemm_prepare(GemmPlan* plan, const void* w, int w_kind, int O, int K, const 
   return 0;
 }
 
-cudaError_t gemm_launch(const GemmPlan& plan, GemmParams p, int splits, cudaStream_t stream) {
+cudaError_t gemm_launch(const GemmPlan& plan, GemmParams p, int splits, cudaStream_t stream, bool pdl) {
   p.O = plan.O;
   p.K = plan.K;
   p.b_tx_bytes = static_cast<uint32_t>(plan.x_box_rows) * kBlockK * 2;
@@ -699,9 +724,9 @@ cudaError_t gemm_launch(const GemmPlan& plan, GemmParams p, int splits, cudaStre
   const int sms = sm_count();
 #define LB_GEMM_CASE(TNV)                                                                  \
   case TNV:                                                                                \
-    return plan.w_kind == kWInt8  ? launch_gemm_t<TNV, kWInt8>(plan, p, splits, sms, stream) \
-           : plan.w_kind == kWF16 ? launch_gemm_t<TNV, kWF16>(plan, p, splits, sms, stream)  \
-                                  : launch_gemm_t<TNV, kWBf16>(plan, p, splits, sms, stream);
+    return plan.w_kind == kWInt8  ? launch_gemm_t<TNV, kWInt8>(plan, p, splits, sms, stream, pdl) \
+           : plan.w_kind == kWF16 ? launch_gemm_t<TNV, kWF16>(plan, p, splits, sms, stream, pdl)  \
+                                  : launch_gemm_t<TNV, kWBf16>(plan, p, splits, sms, stream, pdl);
   switch (plan.tn) {
     LB_GEMM_CASE(32)
     LB_GEMM_CASE(64)

@@ -99,6 +99,8 @@ struct AttnSmem {
 
 template <int HD>
 __global__ void __launch_bounds__(512) attention_kernel(AttnDev a) {
+  pdl_wait();  // first: nothing of the previous kernel is read or written before it
+  pdl_trigger();
   using L = AttnSmem<HD>;
   constexpr int NP = HD / 64;  // bf16 pairs per lane in the value sum (lanes own dimensions)
   constexpr int KS = HD / 16;  // MMA k-steps over the head dimension
@@ -394,10 +396,10 @@ cudaError_t launch_attention(Ctx& c, int layer, int rows_cap, cudaStream_t s) {
   const int threads = 32 * c.cfg.heads;
   const size_t smem = attention_smem_bytes(c.cfg.heads, c.hd);
   switch (c.hd) {
-    case 64: attention_kernel<64><<<rows_cap, threads, smem, s>>>(a); break;
-    case 128: attention_kernel<128><<<rows_cap, threads, smem, s>>>(a); break;
-    case 192: attention_kernel<192><<<rows_cap, threads, smem, s>>>(a); break;
-    case 256: attention_kernel<256><<<rows_cap, threads, smem, s>>>(a); break;
+    case 64: launch_kernel(c.pdl_all, attention_kernel<64>, dim3(rows_cap), dim3(threads), smem, s, a); break;
+    case 128: launch_kernel(c.pdl_all, attention_kernel<128>, dim3(rows_cap), dim3(threads), smem, s, a); break;
+    case 192: launch_kernel(c.pdl_all, attention_kernel<192>, dim3(rows_cap), dim3(threads), smem, s, a); break;
+    case 256: launch_kernel(c.pdl_all, attention_kernel<256>, dim3(rows_cap), dim3(threads), smem, s, a); break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();

@@ -37,6 +37,12 @@ struct MelArgs {
   float* mel;          // [rows][8][128]
   const float *window, *cos_tab, *sin_tab, *filters;  // [320], [512], [512], [257][128]
   const int2* filter_range;                          // [128] (k_lo, k_hi)
+  // Stand-alone form (counts == nullptr): n_static rows, each with its own
+  // caller-held tail [rows][160] (ext_tail_in, nullptr = a fresh stream) and
+  // the new tails written to ext_tail_out; no slot state is touched.
+  int n_static;
+  const float* ext_tail_in;
+  float* ext_tail_out;
 };
 
 // One complex multiply-free radix-4 DFT in place: (x0, x1, x2, x3) ->
@@ -102,6 +108,8 @@ __device__ __forceinline__ void dft16(float (&re)[16], float (&im)[16], const fl
 // one padded shared-memory transpose, and 16-point DFTs again.  Exact twiddles
 // cos/sin(2 pi j / 512) from the table; fp32 throughout.
 __global__ void __launch_bounds__(256) mel_kernel(MelArgs a) {
+  pdl_wait();  // first: nothing of the previous kernel is read or written before it
+  pdl_trigger();
   const int row = blockIdx.x;
   constexpr int kSig = kTail + kPcm;                // padded signal [tail | pcm]
   __shared__ __align__(16) float sig[kSig];         // phases 0-1
@@ -110,14 +118,18 @@ __global__ void __launch_bounds__(256) mel_kernel(MelArgs a) {
   float (*mag)[kBins + 3] = reinterpret_cast<float (*)[kBins + 3]>(&yr[0][0][0]);  // reuses yr/yi
   static_assert(sizeof(yr) + sizeof(yi) >= sizeof(float) * kFrames * (kBins + 3), "mag fits in yr/yi");
   // row tables (in bounds for every row of the bucket) read with the live count
-  const int n_rows = a.counts[0];
-  const int slot = a.row_slot[row];
-  const int parity = (a.row_meta[row].pos >> 1) & 1;
-  const int reason = a.row_reason[row];
+  const bool ext = a.counts == nullptr;
+  const int n_rows = ext ? a.n_static : a.counts[0];
+  const int slot = ext ? 0 : a.row_slot[row];
+  const int parity = ext ? 0 : (a.row_meta[row].pos >> 1) & 1;
+  const int reason = ext ? 0 : a.row_reason[row];
   if (row >= n_rows) return;
-  // identity resets start a fresh session: no previous PCM tail
-  const bool fresh = reason == 3 || reason == 1;
-  const float* tail_in = a.tail + (static_cast<size_t>(slot) * 2 + parity) * kTail;
+  // A new session or identity (identity_reset) and an explicit reset start
+  // from a zero tail; across a cursor gap the session keeps its tail, as the
+  // reference frontend keeps it in the session state.
+  const bool fresh = ext ? a.ext_tail_in == nullptr : (reason == 3 || reason == 1);
+  const float* tail_in = ext ? (a.ext_tail_in ? a.ext_tail_in + static_cast<size_t>(row) * kTail : nullptr)
+                             : a.tail + (static_cast<size_t>(slot) * 2 + parity) * kTail;
   const float* pcm = a.pcm + static_cast<size_t>(row) * kPcm;
   const int tid = threadIdx.x;
   // ---- phase 0: [tail | pcm] into shared memory (16-byte loads), new tail out
@@ -130,7 +142,8 @@ __global__ void __launch_bounds__(256) mel_kernel(MelArgs a) {
     }
     reinterpret_cast<float4*>(sig)[i] = v;
   }
-  float* tail_out = a.tail + (static_cast<size_t>(slot) * 2 + (parity ^ 1)) * kTail;
+  float* tail_out = ext ? a.ext_tail_out + static_cast<size_t>(row) * kTail
+                       : a.tail + (static_cast<size_t>(slot) * 2 + (parity ^ 1)) * kTail;
   for (int i = tid; i < kTail / 4; i += blockDim.x)
     reinterpret_cast<float4*>(tail_out)[i] = __ldg(reinterpret_cast<const float4*>(pcm) + (kPcm - kTail) / 4 + i);
   __syncthreads();
@@ -257,6 +270,8 @@ __device__ __forceinline__ uint32_t pack_f16x2(float x, float y) {
 
 // C1 = 32 output channels (validated at create): 8 warps = 4 position tiles x 2 channel halves.
 __global__ void __launch_bounds__(kSubThreads, 1) subsample_kernel(SubArgs a) {
+  pdl_wait();  // first: nothing of the previous kernel is read or written before it
+  pdl_trigger();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sp = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) &
                                            ~static_cast<uintptr_t>(127));
@@ -504,7 +519,7 @@ constexpr size_t kSubSmem = 128 + 32 * kK1Pad * 2 + 5 * 66 * kCiPad * 2 + 128 * 
 
 cudaError_t launch_mel(Ctx& c, int rows_cap, int input_kind, cudaStream_t s) {
   if (input_kind != LB_INPUT_PCM) return cudaSuccess;  // mel supplied by the caller
-  MelArgs a;
+  MelArgs a = {};
   a.counts = c.dev_counts;
   a.row_slot = c.row_slot;
   a.row_reason = c.row_reason;
@@ -517,7 +532,25 @@ cudaError_t launch_mel(Ctx& c, int rows_cap, int input_kind, cudaStream_t s) {
   a.sin_tab = c.fe_sin;
   a.filters = c.fe_filters;
   a.filter_range = c.fe_range;
-  mel_kernel<<<rows_cap, 256, 0, s>>>(a);
+  launch_kernel(c.pdl_all, mel_kernel, dim3(rows_cap), dim3(256), 0, s, a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_mel_standalone(Ctx& c, int n, const float* pcm, const float* tail_in, float* tail_out,
+                                  float* mel, cudaStream_t s) {
+  MelArgs a = {};
+  a.counts = nullptr;
+  a.n_static = n;
+  a.pcm = pcm;
+  a.ext_tail_in = tail_in;
+  a.ext_tail_out = tail_out;
+  a.mel = mel;
+  a.window = c.fe_window;
+  a.cos_tab = c.fe_cos;
+  a.sin_tab = c.fe_sin;
+  a.filters = c.fe_filters;
+  a.filter_range = c.fe_range;
+  mel_kernel<<<n, 256, 0, s>>>(a);
   return cudaGetLastError();
 }
 
@@ -544,7 +577,7 @@ cudaError_t launch_subsample(Ctx& c, int rows_cap, cudaStream_t s) {
   a.eps = c.cfg.rms_eps;
   a.c1 = c.cfg.sub_ch1;
   int grid = rows_cap < c.num_sms ? rows_cap : c.num_sms;
-  subsample_kernel<<<grid, kSubThreads, kSubSmem, s>>>(a);
+  launch_kernel(c.pdl_all, subsample_kernel, dim3(grid), dim3(kSubThreads), kSubSmem, s, a);
   return cudaGetLastError();
 }
 

@@ -13,7 +13,6 @@
 //   lconv_kernel       GLU -> causal depthwise conv (k=5) over the conv-state
 //                      ring -> clamp -> RMSNorm -> SiLU -> bf16; stages the 2 new
 //                      GLU rows (streaming_conformer.py:830-852, modeling_gemma4.py:444-482)
-//   finalize_wide      split-K accumulator -> (SiLU) -> bf16
 //   outputs / film     output_proj + embed_audio tails and the FiLM elementwise
 //                      stages (streaming_conformer.py:871-872,
 //                      frame_residual_adapter.py:203-234)
@@ -132,6 +131,8 @@ struct RowFusedDev {
 // 2048-token step in one wave.
 template <int G>
 __global__ void __launch_bounds__(128, 4) row_fused_kernel(RowFusedDev a) {
+  pdl_wait();  // first: nothing of the previous kernel is read or written before it
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int t = blockIdx.x * 4 + (threadIdx.x >> 5);  // the grid covers the bucket's tokens exactly
   constexpr int d = G * 256;
@@ -253,6 +254,8 @@ struct LconvDev {
 // in one wave of 256-thread CTAs.
 template <int G, int W>
 __global__ void __launch_bounds__(256) lconv_kernel(LconvDev a) {
+  pdl_wait();  // first: nothing of the previous kernel is read or written before it
+  pdl_trigger();
   constexpr int GW = G / W;  // channel groups per warp
   static_assert(G % W == 0, "channel groups must split evenly over the session's warps");
   __shared__ float2 part[8];  // per warp: (sum sq token 0, sum sq token 1)
@@ -342,27 +345,35 @@ __global__ void __launch_bounds__(256) lconv_kernel(LconvDev a) {
   }
 }
 
-// ------------------------------------------------------- split-K finalize
-__global__ void finalize_wide_kernel(const int* counts, const float* acc, int width, int act,
-                                     __nv_bfloat16* out, FinalizeClip fc, bool f16) {
+// --------------------------------------------------------- split-K finish
+__global__ void split_finish_kernel(const int* m_dev, int m_static, float* acc, int width, int act, void* out,
+                                    int ld_out, int out_f32, FinalizeClip fc, bool f16) {
+  pdl_wait();  // the GEMM's partial sums are complete
+  pdl_trigger();
   const int t = blockIdx.y;
-  if (t >= counts[1]) return;
+  if (t >= (m_dev ? *m_dev : m_static)) return;
   const int o = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
   if (o >= width) return;
   // stacked parts: 8 consecutive features never straddle a part (part_o % 128 == 0)
   const int j = fc.part_o ? o / fc.part_o : 0;
   const float lo = j == 0 ? fc.lo[0] : j == 1 ? fc.lo[1] : fc.lo[2];
   const float hi = j == 0 ? fc.hi[0] : j == 1 ? fc.hi[1] : fc.hi[2];
-  const float plo = fc.plo, phi = fc.phi;
+  float* a = acc + static_cast<size_t>(t) * width + o;
   float v[8];
-  load8(acc + static_cast<size_t>(t) * width + o, v);
+  load8(a, v);
+  const float z[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  store8(a, z);
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     float y = fminf(fmaxf(v[i], lo), hi);
     if (act == 1) y = silu_f(bf16_round(y));
-    v[i] = fminf(fmaxf(y, plo), phi);
+    v[i] = fminf(fmaxf(y, fc.plo), fc.phi);
   }
-  store8_act(out + static_cast<size_t>(t) * width + o, v, f16);
+  if (out_f32) {
+    store8(static_cast<float*>(out) + static_cast<size_t>(t) * ld_out + o, v);
+  } else {
+    store8_act(static_cast<__nv_bfloat16*>(out) + static_cast<size_t>(t) * ld_out + o, v, f16);
+  }
 }
 
 // ----------------------------------------------------------- output tails
@@ -371,6 +382,8 @@ __global__ void finalize_wide_kernel(const int* counts, const float* acc, int wi
 __global__ void __launch_bounds__(256) outputs_kernel(const int* counts, const float* y, int width,
                                                      int stage, __nv_bfloat16* out,
                                                      __nv_bfloat16* next_in, float eps, bool f16) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float sh[32];
   const int t = blockIdx.x;
   if (t >= counts[1]) return;
@@ -393,6 +406,8 @@ __global__ void __launch_bounds__(256) film_norm_kernel(const int* counts, const
                                                        const float* hw, const float* hb,
                                                        __nv_bfloat16* xq, __nv_bfloat16* xr,
                                                        float* amp, bool f16) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float sh[32];
   const int t = blockIdx.x;
   if (t >= counts[1]) return;
@@ -433,6 +448,8 @@ __global__ void __launch_bounds__(256) film_norm_kernel(const int* counts, const
 // FiLM stage 1: fused = SiLU(qd * (1 + tanh(gamma)) + beta) -> bf16
 __global__ void film_fuse_kernel(const int* counts, const float* qd, const float* gb, int bdim,
                                  __nv_bfloat16* fused, bool f16) {
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.x;
   if (t >= counts[1]) return;
   for (int e = threadIdx.x; e < bdim; e += blockDim.x) {
@@ -446,6 +463,8 @@ __global__ void film_fuse_kernel(const int* counts, const float* qd, const float
 // FiLM stage 2: out = query + tanh(mapped) * scale * RMS(query)
 __global__ void film_out_kernel(const int* counts, const float* mapped, const __nv_bfloat16* query,
                                 const float* amp, int qdim, float scale, __nv_bfloat16* out) {
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.y;
   if (t >= counts[1]) return;
   const int e = blockIdx.x * blockDim.x + threadIdx.x;
@@ -486,13 +505,13 @@ cudaError_t launch_row_fused(Ctx& c, int tok_cap, const RowFusedArgs& r, cudaStr
   if (r.xa_parts != 1 && (r.xa_parts != 3 || r.xa != c.xa)) return cudaErrorInvalidValue;
   const int grid = tok_cap / 4;  // four tokens (warps) per CTA; tok_cap is a multiple of 32
   switch (c.cfg.hidden / 256) {
-    case 1: row_fused_kernel<1><<<grid, 128, 0, s>>>(a); break;
-    case 2: row_fused_kernel<2><<<grid, 128, 0, s>>>(a); break;
-    case 3: row_fused_kernel<3><<<grid, 128, 0, s>>>(a); break;
-    case 4: row_fused_kernel<4><<<grid, 128, 0, s>>>(a); break;
-    case 5: row_fused_kernel<5><<<grid, 128, 0, s>>>(a); break;
-    case 6: row_fused_kernel<6><<<grid, 128, 0, s>>>(a); break;
-    case 8: row_fused_kernel<8><<<grid, 128, 0, s>>>(a); break;
+    case 1: launch_kernel(c.pdl_all, row_fused_kernel<1>, dim3(grid), dim3(128), 0, s, a); break;
+    case 2: launch_kernel(c.pdl_all, row_fused_kernel<2>, dim3(grid), dim3(128), 0, s, a); break;
+    case 3: launch_kernel(c.pdl_all, row_fused_kernel<3>, dim3(grid), dim3(128), 0, s, a); break;
+    case 4: launch_kernel(c.pdl_all, row_fused_kernel<4>, dim3(grid), dim3(128), 0, s, a); break;
+    case 5: launch_kernel(c.pdl_all, row_fused_kernel<5>, dim3(grid), dim3(128), 0, s, a); break;
+    case 6: launch_kernel(c.pdl_all, row_fused_kernel<6>, dim3(grid), dim3(128), 0, s, a); break;
+    case 8: launch_kernel(c.pdl_all, row_fused_kernel<8>, dim3(grid), dim3(128), 0, s, a); break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();
@@ -523,50 +542,100 @@ cudaError_t launch_lconv(Ctx& c, int layer, int rows_cap, cudaStream_t s) {
   const int per_cta = g % 2 == 0 ? 4 : 8;
   const int grid = (rows_cap + per_cta - 1) / per_cta;
   switch (g) {
-    case 1: lconv_kernel<1, 1><<<grid, 256, 0, s>>>(a); break;
-    case 2: lconv_kernel<2, 2><<<grid, 256, 0, s>>>(a); break;
-    case 3: lconv_kernel<3, 1><<<grid, 256, 0, s>>>(a); break;
-    case 4: lconv_kernel<4, 2><<<grid, 256, 0, s>>>(a); break;
-    case 5: lconv_kernel<5, 1><<<grid, 256, 0, s>>>(a); break;
-    case 6: lconv_kernel<6, 2><<<grid, 256, 0, s>>>(a); break;
-    case 8: lconv_kernel<8, 2><<<grid, 256, 0, s>>>(a); break;
+    case 1: launch_kernel(c.pdl_all, lconv_kernel<1, 1>, dim3(grid), dim3(256), 0, s, a); break;
+    case 2: launch_kernel(c.pdl_all, lconv_kernel<2, 2>, dim3(grid), dim3(256), 0, s, a); break;
+    case 3: launch_kernel(c.pdl_all, lconv_kernel<3, 1>, dim3(grid), dim3(256), 0, s, a); break;
+    case 4: launch_kernel(c.pdl_all, lconv_kernel<4, 2>, dim3(grid), dim3(256), 0, s, a); break;
+    case 5: launch_kernel(c.pdl_all, lconv_kernel<5, 1>, dim3(grid), dim3(256), 0, s, a); break;
+    case 6: launch_kernel(c.pdl_all, lconv_kernel<6, 2>, dim3(grid), dim3(256), 0, s, a); break;
+    case 8: launch_kernel(c.pdl_all, lconv_kernel<8, 2>, dim3(grid), dim3(256), 0, s, a); break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();
 }
 
-cudaError_t launch_finalize_wide(Ctx& c, int tok_cap, const float* acc, int width, int act,
-                                 __nv_bfloat16* out, const FinalizeClip& fc, bool out_f16,
-                                 cudaStream_t s) {
-  if (fc.part_o < 0 || (fc.part_o && (fc.part_o % 128 || width / fc.part_o > 3)))
+cudaError_t launch_split_finish(const int* m_dev, int m_static, int m_cap, float* acc, int width, int act,
+                                void* out, int ld_out, bool out_f32, bool f16, const FinalizeClip& fc,
+                                bool pdl, cudaStream_t s) {
+  if (width % 8 || ld_out % 8 || fc.part_o < 0 || (fc.part_o && (fc.part_o % 128 || width / fc.part_o > 3)))
     return cudaErrorInvalidValue;
   const int per_block = 128 * 8;
-  dim3 grid((width + per_block - 1) / per_block, tok_cap);
-  finalize_wide_kernel<<<grid, 128, 0, s>>>(c.dev_counts, acc, width, act, out, fc, out_f16);
+  dim3 grid((width + per_block - 1) / per_block, m_cap);
+  launch_kernel(pdl, split_finish_kernel, grid, dim3(128), 0, s, m_dev, m_static, acc, width, act, out, ld_out,
+                out_f32 ? 1 : 0, fc, f16);
   return cudaGetLastError();
 }
 
 cudaError_t launch_outputs(Ctx& c, int tok_cap, int stage, cudaStream_t s) {
   const int width = stage == 0 ? c.cfg.output_dims : c.cfg.text_hidden;
-  outputs_kernel<<<tok_cap, width / 8, 0, s>>>(c.dev_counts, c.y, width, stage,
+  launch_kernel(c.pdl_all, outputs_kernel, dim3(tok_cap), dim3(width / 8), 0, s, c.dev_counts, c.y, width, stage,
                                                stage == 0 ? c.out_raw : c.out_soft, c.xe,
                                                c.cfg.rms_eps, c.f16_acts != 0);
+  return cudaGetLastError();
+}
+
+// Talker placement of the FiLM adapter (apply_response_state_residual,
+// duplex_kernel/frame_residual_adapter.py:38-71): row i takes response state
+// min(step, n_states - 1) of its [max_states][hdim] response hidden (the
+// Qwen text cursor; the last state is held once the text is exhausted) and
+// its query into the FiLM inputs, and sets the FiLM token count to n.
+__global__ void __launch_bounds__(256) film_talker_gather_kernel(
+    int n, const __nv_bfloat16* hidden, int max_states, const int* n_states, const int* steps,
+    const __nv_bfloat16* query, int hdim, int qdim, __nv_bfloat16* soft, __nv_bfloat16* in_query, int* counts,
+    int* status) {
+  const int i = blockIdx.x;
+  if (i == 0 && threadIdx.x == 0) counts[1] = n;
+  const int ns = n_states[i], st = steps[i];
+  if (ns < 1 || ns > max_states || st < 0) {
+    if (threadIdx.x == 0) atomicOr(status, kStatusBadRowCount);
+    return;
+  }
+  const int idx = min(st, ns - 1);
+  const int4* src = reinterpret_cast<const int4*>(hidden + (static_cast<size_t>(i) * max_states + idx) * hdim);
+  int4* dst = reinterpret_cast<int4*>(soft + static_cast<size_t>(i) * hdim);
+  for (int e = threadIdx.x; e < hdim / 8; e += blockDim.x) dst[e] = src[e];
+  const int4* qs = reinterpret_cast<const int4*>(query + static_cast<size_t>(i) * qdim);
+  int4* qd = reinterpret_cast<int4*>(in_query + static_cast<size_t>(i) * qdim);
+  for (int e = threadIdx.x; e < qdim / 8; e += blockDim.x) qd[e] = qs[e];
+}
+
+// out = query at the first generation step (the query FiLM adapter's
+// preserve_frame0), the conditioned query otherwise.
+__global__ void __launch_bounds__(256) film_talker_finish_kernel(int n, const int* steps, const __nv_bfloat16* query,
+                                                                 const __nv_bfloat16* film, int qdim,
+                                                                 __nv_bfloat16* out) {
+  const int i = blockIdx.x;
+  const bool keep = steps[i] == 0;
+  const int4* src = reinterpret_cast<const int4*>((keep ? query : film) + static_cast<size_t>(i) * qdim);
+  int4* dst = reinterpret_cast<int4*>(out + static_cast<size_t>(i) * qdim);
+  for (int e = threadIdx.x; e < qdim / 8; e += blockDim.x) dst[e] = src[e];
+}
+
+cudaError_t launch_film_talker(Ctx& c, int n, const __nv_bfloat16* hidden, int max_states, const int* n_states,
+                               const int* steps, const __nv_bfloat16* query, __nv_bfloat16* out, int stage,
+                               cudaStream_t s) {
+  const int Q = c.cfg.film_query_dim, T = c.cfg.text_hidden;
+  if (stage == 0)
+    film_talker_gather_kernel<<<n, 256, 0, s>>>(n, hidden, max_states, n_states, steps, query, T, Q, c.out_soft,
+                                                 c.in_query, c.dev_counts, c.status);
+  else
+    film_talker_finish_kernel<<<n, 256, 0, s>>>(n, steps, query, c.out_film, Q, out);
   return cudaGetLastError();
 }
 
 cudaError_t launch_film(Ctx& c, int tok_cap, int stage, cudaStream_t s) {
   const int Q = c.cfg.film_query_dim, B = c.cfg.film_bottleneck, T = c.cfg.text_hidden;
   if (stage == 0) {
-    film_norm_kernel<<<tok_cap, 128, 0, s>>>(c.dev_counts, c.in_query, Q, c.out_soft, T,
+    launch_kernel(c.pdl_all, film_norm_kernel, dim3(tok_cap), dim3(128), 0, s, c.dev_counts, c.in_query, Q, c.out_soft, T,
                                              c.w.fq_norm_w, c.w.fq_norm_b, c.w.fr_norm_w,
                                              c.w.fr_norm_b, c.film_xq, c.film_xr, c.film_amp,
                                              c.f16_acts != 0);
   } else if (stage == 1) {
-    film_fuse_kernel<<<tok_cap, 128, 0, s>>>(c.dev_counts, c.film_qd, c.film_gb, B, c.film_fused,
+    launch_kernel(c.pdl_all, film_fuse_kernel, dim3(tok_cap), dim3(128), 0, s, c.dev_counts, c.film_qd, c.film_gb, B, c.film_fused,
                                              c.f16_acts != 0);
   } else {
     dim3 grid((Q + 255) / 256, tok_cap);
-    film_out_kernel<<<grid, 256, 0, s>>>(c.dev_counts, c.film_map, c.in_query, c.film_amp, Q,
+    launch_kernel(c.pdl_all, film_out_kernel, dim3(grid), dim3(256), 0, s, c.dev_counts, c.film_map, c.in_query, c.film_amp, Q,
                                          c.w.film_scale, c.out_film);
   }
   return cudaGetLastError();

@@ -71,7 +71,24 @@ int gemm_prepare(GemmPlan* plan, const void* w, int w_kind, int O, int K, const 
 cudaError_t widen_int8_codes(const void* src, void* dst, size_t n, cudaStream_t stream);
 // dst[i] = fp16(src[i]) for n bf16 values (n % 8 == 0, 16-byte aligned), saturating.
 cudaError_t widen_bf16_to_f16(const void* src, void* dst, size_t n, cudaStream_t stream);
-cudaError_t gemm_launch(const GemmPlan& plan, GemmParams p, int splits, cudaStream_t stream);
+// Clamps of the split-K finish pass: output clamp per stacked part (part_o
+// features each; part_o = 0: one part, lo[0]/hi[0]) and the next input clamp.
+struct FinalizeClip {
+  int part_o = 0;
+  float lo[3] = {-INFINITY, -INFINITY, -INFINITY}, hi[3] = {INFINITY, INFINITY, INFINITY};
+  float plo = -INFINITY, phi = INFINITY;
+};
+// Finishes a split-K GEMM whose K slices were reduce-added into acc (fp32
+// [rows][width], out_mode 2): rows below *m_dev (or m_static when m_dev is
+// null) get the output clamp, SiLU (act 1, of the bf16-rounded sum) and the
+// next-input clamp and are stored to out ([rows][ld_out]; out_f32: fp32, else
+// bf16, or fp16 with f16); the accumulator is zeroed behind the read, so it is
+// ready for the next split-K GEMM without a memset.
+cudaError_t launch_split_finish(const int* m_dev, int m_static, int m_cap, float* acc, int width, int act,
+                                void* out, int ld_out, bool out_f32, bool f16, const FinalizeClip& fc,
+                                bool pdl, cudaStream_t s);
+// pdl: launch with programmatic stream serialisation (common.cuh pdl_wait).
+cudaError_t gemm_launch(const GemmPlan& plan, GemmParams p, int splits, cudaStream_t stream, bool pdl = false);
 // K-split count that fills the SMs for an [m_cap x O] output with K reduction.
 int gemm_pick_splits(int O, int K, int m_cap, int num_sms);
 

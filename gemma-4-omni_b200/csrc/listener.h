@@ -125,6 +125,9 @@ struct GemmOp {
   GemmParams params;
   int splits = 1;
   bool final_f16 = false;  // output feeds another GEMM in fp16 (int8 weights)
+  bool pdl = false;        // launched with programmatic stream serialisation
+  int out_kind = 0;        // 0: bf16 / fp16 tensor, 1: fp32 (the split-K finish pass's store)
+  void* out = nullptr;     // the op's output (a split-K GEMM itself writes wide_acc)
 };
 
 struct Bucket {
@@ -144,6 +147,12 @@ struct Ctx {
   // fp16 exactly, and every activation that feeds a GEMM is stored as fp16
   // (saturated at +/-65504), 3 more mantissa bits than bf16
   int f16_acts = 1;
+  // Programmatic dependent launch of the step's kernels (common.cuh pdl_wait).
+  // pdl: GEMMs launch while the kernel before them drains and stream their
+  // first weight tiles meanwhile; pdl_all: every other step kernel launches
+  // early too.  LB_PDL=0 / 1 / 2: off / GEMMs only / all kernels.
+  bool pdl = true;
+  bool pdl_all = false;
 
   // arenas
   void* weight_arena = nullptr;
@@ -207,7 +216,8 @@ struct Ctx {
   __nv_bfloat16* qkv = nullptr;       // [tok][3d]
   __nv_bfloat16* att = nullptr;       // [tok][d]
   __nv_bfloat16* gl = nullptr;        // [tok][2d] linear_start output
-  float* wide_acc = nullptr;          // [tok][max(F,3d,2d)] split-K accumulators
+  float* wide_acc = nullptr;          // [tok][max(F,3d,2d)] split-K partial sums (kept zero)
+  int wide_width = 0;                 // row width of wide_acc
   __nv_bfloat16* out_raw = nullptr;   // [tok][out]
   __nv_bfloat16* out_soft = nullptr;  // [tok][text]
   __nv_bfloat16* out_film = nullptr;  // [tok][Q]
@@ -238,6 +248,9 @@ struct Ctx {
 
 // --------------------------------------------------------- kernel launchers
 cudaError_t launch_mel(Ctx& c, int rows_cap, int input_kind, cudaStream_t s);
+// The log-mel of n caller rows with caller-held tails (no session state).
+cudaError_t launch_mel_standalone(Ctx& c, int n, const float* pcm, const float* tail_in, float* tail_out,
+                                  float* mel, cudaStream_t s);
 cudaError_t launch_subsample(Ctx& c, int rows_cap, cudaStream_t s);
 cudaError_t launch_pack(Ctx& c, int n_rows, long long step_id, cudaStream_t s);
 cudaError_t launch_commit(Ctx& c, cudaStream_t s);
@@ -265,21 +278,17 @@ struct RowFusedArgs {
   int xa_parts = 1;
   float part_lo[2] = {-INFINITY, -INFINITY}, part_hi[2] = {INFINITY, INFINITY};
 };
-// Clamps of the split-K finalize pass: output clamp per stacked part (part_o
-// features each; part_o = 0: one part, lo[0]/hi[0]) and the next input clamp.
-struct FinalizeClip {
-  int part_o = 0;
-  float lo[3] = {-INFINITY, -INFINITY, -INFINITY}, hi[3] = {INFINITY, INFINITY, INFINITY};
-  float plo = -INFINITY, phi = INFINITY;
-};
 cudaError_t launch_row_fused(Ctx& c, int tok_cap, const RowFusedArgs& a, cudaStream_t s);
 cudaError_t launch_attention(Ctx& c, int layer, int rows_cap, cudaStream_t s);
 // bf16 copies of every layer's relative keys (after the weights are uploaded).
 cudaError_t attention_prepare(Ctx& c, cudaStream_t s);
 cudaError_t launch_lconv(Ctx& c, int layer, int rows_cap, cudaStream_t s);
-cudaError_t launch_finalize_wide(Ctx& c, int tok_cap, const float* acc, int width, int act,
-                                 __nv_bfloat16* out, const FinalizeClip& clip, bool out_f16, cudaStream_t s);
 cudaError_t launch_outputs(Ctx& c, int tok_cap, int stage, cudaStream_t s);
 cudaError_t launch_film(Ctx& c, int tok_cap, int stage, cudaStream_t s);
+// stage 0: gather the cursor-selected response states and queries into the
+// FiLM inputs; stage 1: write the outputs (frame 0 preserved)
+cudaError_t launch_film_talker(Ctx& c, int n, const __nv_bfloat16* hidden, int max_states, const int* n_states,
+                               const int* steps, const __nv_bfloat16* query, __nv_bfloat16* out, int stage,
+                               cudaStream_t s);
 
 }  // namespace lb

@@ -19,12 +19,16 @@ which the streaming tower reads the last 8 rows (:498-555).  Here the rows'
 80 ms PCM frames ([N, 1280] float32, 5 KB per row) are copied once from a
 pinned staging buffer and the tower's ``prepare_batch_pcm`` runs the log-mel
 inside the step, with each session's 160-sample tail kept in its state slot
-and advanced by the same commit as the rest of its state.  The tail restarts
-from zeros whenever the tower's state does (any reset reason other than
-``continue``); the reference frontend keeps a session's tail in its
-``ListenerSessionState`` across a tower-side cursor-gap reset, so the first
-mel row after such a gap differs.  No W240 window, per-row runner fallback or
-host mel history is kept: the streaming tower is the only execution path.
+and advanced by the same commit as the rest of its state.  A new session or
+identity starts from a zero tail; across a cursor gap the session keeps its
+tail, as the reference keeps it in the session state.  The assistant
+(reference) audio of every row is turned into mel as well, as the reference
+does for its history (:792-809): all rows in one GPU pass (``lb_mel_async``)
+with each session's assistant tail held on the device and advanced on commit;
+``PreparedListenerAudioBatch.assistant_mels`` is that [N, 8, 128] tensor (a
+row without reference audio uses silence, as in the reference).  No W240
+window, per-row runner fallback or host mel history is kept: the streaming
+tower is the only execution path.
 
 The batch and state objects are the reference's contracts
 (duplex_kernel/microbatch_contract.py), used by attribute: ``batch.manifest``
@@ -61,8 +65,11 @@ class PreparedListenerAudioBatch:
 
     def __init__(self, *, owner: "ListenerMicrobatchAudioFrontend", manifest_id: str, n: int,
                  streaming_batch, cursors: tuple, frontend_copy_ms: float, frontend_copy_events,
-                 tower_events, graph_submit_ms: float, owner_thread_id: int) -> None:
+                 tower_events, graph_submit_ms: float, owner_thread_id: int,
+                 assistant_mels: torch.Tensor, assistant_tails: torch.Tensor) -> None:
         self._owner = owner
+        self.assistant_mels = assistant_mels
+        self._assistant_tails = assistant_tails
         self.manifest_id = manifest_id
         self.input_shape = (n, MEL_ROWS_PER_FRAME, MEL_BINS)
         self.streaming_audio_input_shape = (n, MEL_ROWS_PER_FRAME, MEL_BINS)
@@ -113,6 +120,8 @@ class PreparedListenerAudioBatch:
             self._aborted = True
             self._owner._finish(self.manifest_id, failed=True)
             raise
+        for i, cursor in enumerate(self.audio_stream_cursors):
+            self._owner._assistant_tails[cursor.session_id] = self._assistant_tails[i]
         self._committed = True
         self._owner._finish(self.manifest_id, failed=False)
 
@@ -162,6 +171,7 @@ class ListenerMicrobatchAudioFrontend:
         self._closed = False
         self._pinned: torch.Tensor | None = None
         self._copy_done: torch.cuda.Event | None = None
+        self._assistant_tails: dict[str, torch.Tensor] = {}  # session -> device [160] float32
         self.encoder_call_count = 0
 
     # ------------------------------------------------------------ lifetime
@@ -180,6 +190,7 @@ class ListenerMicrobatchAudioFrontend:
             if self._active_manifest_id is not None:
                 raise RuntimeError("cannot close streaming audio state while a batch is prepared")
             self.streaming_audio_tower.reset(session_id)
+            self._assistant_tails.pop(session_id, None)
         finally:
             self._call_lock.release()
 
@@ -211,9 +222,11 @@ class ListenerMicrobatchAudioFrontend:
             self._copy_done.synchronize()
             self._copy_done = None
         if self._pinned is None or self._pinned.shape[0] < n:
-            cap = max(n, 2 * (self._pinned.shape[0] if self._pinned is not None else 0), 16)
-            self._pinned = torch.empty((cap, PCM_SAMPLES_PER_FRAME), dtype=torch.float32, pin_memory=True)
-        return self._pinned[:n]
+            cap = max(n, 2 * (self._pinned.shape[0] // 2 if self._pinned is not None else 0), 16)
+            # rows [0, cap): user PCM; rows [cap, 2 cap): assistant (reference) PCM
+            self._pinned = torch.empty((2 * cap, PCM_SAMPLES_PER_FRAME), dtype=torch.float32, pin_memory=True)
+        cap = self._pinned.shape[0] // 2
+        return self._pinned[:n], self._pinned[cap:cap + n]
 
     # ----------------------------------------------------------- the tick
     def encode_batch(self, batch: Any, states: Sequence[Any], *,
@@ -243,12 +256,20 @@ class ListenerMicrobatchAudioFrontend:
                     raise RuntimeError("frontend row does not match its current session snapshot")
             stream = listener_stream if listener_stream is not None else torch.cuda.current_stream(self.device)
             copy_started = time.perf_counter_ns()
-            host = self._staging(n)
+            host, host_ref = self._staging(n)
             for i, frame in enumerate(batch.frames):
                 pcm = np.asarray(frame.pcm, dtype=np.float32)
                 if pcm.shape != (PCM_SAMPLES_PER_FRAME,):
                     raise ValueError("listener frames must carry 1280 PCM samples")
                 host[i].numpy()[:] = pcm
+                ref = getattr(frame, "reference_pcm", None)
+                if ref is None:
+                    host_ref[i].numpy()[:] = 0.0  # no assistant audio: silence, as the reference
+                else:
+                    ref = np.asarray(ref, dtype=np.float32)
+                    if ref.shape != (PCM_SAMPLES_PER_FRAME,):
+                        raise ValueError("reference frames must carry 1280 PCM samples")
+                    host_ref[i].numpy()[:] = ref
             cursors = tuple(AudioStreamCursor(session_id=row.session_id, generation_id=int(row.session_generation),
                                               state_epoch_id=row.state_epoch_id, frame_id=int(row.frame_id),
                                               sequence_position=int(row.sequence_position))
@@ -260,7 +281,14 @@ class ListenerMicrobatchAudioFrontend:
                     tower_ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                     copy_ev[0].record(stream)
                     pcm_dev = host.to(self.device, non_blocking=True)
+                    ref_dev = host_ref.to(self.device, non_blocking=True)
                     copy_ev[1].record(stream)
+                    zero = torch.zeros(160, dtype=torch.float32, device=self.device)
+                    tail_in = torch.stack([self._assistant_tails.get(s.session_id, zero) for s in rows])
+                    tail_out = torch.empty((n, 160), dtype=torch.float32, device=self.device)
+                    assistant_mels = torch.empty((n, MEL_ROWS_PER_FRAME, MEL_BINS), dtype=torch.float32,
+                                                 device=self.device)
+                    self.streaming_audio_tower._engine.mel(ref_dev, tail_in, tail_out, assistant_mels)
                     frontend_copy_ms = (time.perf_counter_ns() - copy_started) / 1e6
                     self.encoder_call_count += 1
                     submit = time.perf_counter_ns()
@@ -280,4 +308,5 @@ class ListenerMicrobatchAudioFrontend:
                                               frontend_copy_ms=round(frontend_copy_ms, 3),
                                               frontend_copy_events=copy_ev, tower_events=tower_ev,
                                               graph_submit_ms=round(graph_submit_ms, 3),
-                                              owner_thread_id=current)
+                                              owner_thread_id=current, assistant_mels=assistant_mels,
+                                              assistant_tails=tail_out)

@@ -172,6 +172,20 @@ class ListenerEngine:
         _lib.check("lb_get_status", self.lib.lb_get_status(self._ctx, ctypes.addressof(v), self._stream))
         return int(v.value)
 
+    def mel(self, pcm: torch.Tensor, tail_in: torch.Tensor | None, tail_out: torch.Tensor,
+            mel_out: torch.Tensor) -> None:
+        """lb_mel_async: log-mel of [n,1280] float32 frames with caller-held
+        [n,160] tails (None: fresh streams) into [n,8,128]; asynchronous."""
+        n = int(pcm.shape[0])
+        for t, shape in ((pcm, (n, 1280)), (tail_out, (n, 160)), (mel_out, (n, 8, 128))):
+            if t.dtype != torch.float32 or tuple(t.shape) != shape or not t.is_contiguous() or t.device != self.device:
+                raise ValueError(f"mel tensors must be contiguous float32 {shape} on the engine's device")
+        if tail_in is not None and (tail_in.dtype != torch.float32 or tuple(tail_in.shape) != (n, 160)
+                                    or not tail_in.is_contiguous() or tail_in.device != self.device):
+            raise ValueError("tail_in must be a contiguous float32 [n,160] tensor on the engine's device")
+        _lib.check("lb_mel_async", self.lib.lb_mel_async(self._ctx, n, pcm.data_ptr(), _ptr(tail_in),
+                                                         tail_out.data_ptr(), mel_out.data_ptr(), self._stream))
+
     def counters(self) -> dict[str, int]:
         """lb_get_counters as a dict (synchronises the current stream)."""
         c = _lib.LbCounters()

@@ -180,6 +180,32 @@ int lb_reset_slot_async(lb_ctx* ctx, int32_t slot, void* stream);
 /* Kernels launched by the CUDA graph of the last lb_step_async (0 if eager). */
 int lb_step_kernel_count(lb_ctx* ctx);
 
+/* The reference's incremental log-mel (_extract_single_frame,
+ * duplex_kernel/listener.py:1807-1850) for n PCM frames of any streams whose
+ * tails the caller holds, outside the session state: e.g. the assistant
+ * (reference) audio the frontend turns into mel per row
+ * (listener_microbatch_frontend.py:792-809).  pcm f32 [n][1280]; tail_in f32
+ * [n][160] (NULL: every stream starts fresh); tail_out f32 [n][160] receives
+ * each frame's last 160 samples (must not alias tail_in); mel_out f32
+ * [n][8][128].  Device pointers; asynchronous on `stream`. */
+int lb_mel_async(lb_ctx* ctx, int n, const float* pcm, const float* tail_in, float* tail_out,
+                 float* mel_out, void* stream);
+
+/* The FrameResidualQueryFiLM adapter at its Talker call site, batched over n
+ * sessions: apply_response_state_residual
+ * (duplex_kernel/frame_residual_adapter.py:38-71, called at engine.py:6757).
+ * Row i selects response state min(steps[i], n_states[i] - 1) of its response
+ * hidden (bf16 [max_states][text_hidden], rows max_states apart) -- the Qwen
+ * text cursor, holding the last state once the text is exhausted -- and
+ * conditions its Qwen Q1 query (bf16 [film_query_dim]); at steps[i] == 0 the
+ * query is returned unchanged (the adapter's preserve_frame0).  out bf16
+ * [n][film_query_dim].  n_states / steps: int32 device arrays.  n <= 2 *
+ * max_rows.  Not valid between lb_pack_async and its commit / abort; an
+ * invalid n_states or step sets LB_DEV_BAD_ROW_COUNT. */
+int lb_film_talker_async(lb_ctx* ctx, int n, const void* response_hidden, int max_states,
+                         const int32_t* n_states, const int32_t* steps, const void* query, void* out,
+                         void* stream);
+
 /* Synchronous reads (they synchronise the given stream). */
 int lb_get_status(lb_ctx* ctx, int32_t* status_out, void* stream);
 /* Asynchronous: clears the status word, keeping its bits in the history
@@ -253,12 +279,17 @@ int lb_op_gemm(const void* x, int x_ld, int m, const void* w, int w_int8, const 
  * (parts > 1, >= m): part j reads its activations from x rows
  * [j*x_part_rows, j*x_part_rows + m) (per-part input clamps applied by the
  * producer of x); 0: every part reads rows [0, m).  Finite bounds need
- * out_mode 0 or 1 (split-K partial sums are not clamped). */
+ * out_mode 0 or 1 (out_mode 2 accumulates unclamped partial sums).
+ * splits > 1 with out_mode 0 or 1: the K slices reduce-add into split_acc
+ * (fp32 [m][out_features], zero on entry), then a finish pass applies the
+ * bounds / SiLU, stores `out` and zeroes split_acc again -- how the listener
+ * step runs its small-batch GEMMs.  split_acc may be NULL when splits == 1 or
+ * out_mode == 2. */
 int lb_op_gemm_clipped(const void* x, int x_ld, int m, int x_part_rows, const void* w, int w_int8,
                        const void* w_scale, const float* bias, int out_features, int k, void* out,
                        int ld_out, int out_mode, int act, int splits, int parts,
-                       const float* out_bounds, const float* post_bounds, int* status_dev,
-                       void* stream);
+                       const float* out_bounds, const float* post_bounds, float* split_acc,
+                       int* status_dev, void* stream);
 
 /* ----------------------------------------------------------------------
  * Tick-level row selection (device arrays, asynchronous on `stream`).

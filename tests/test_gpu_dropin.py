@@ -361,6 +361,38 @@ def test_frontend_encode_batch_matches_reference_pcm_golden(pkg):
     fe.close()
 
 
+def test_frontend_assistant_mel_matches_reference_extractor(modules):
+    """The assistant (reference) audio of each row becomes mel on the GPU with
+    its tail carried per session across committed ticks; rows without
+    reference audio use silence (listener_microbatch_frontend.py:792-809)."""
+    from gemma4_omni_b200 import synthetic
+    from gemma4_omni_b200.listener_frontend import ListenerMicrobatchAudioFrontend
+    from oracle import mel_ref
+
+    fe = ListenerMicrobatchAudioFrontend(None, None, device="cuda", dtype=torch.bfloat16,
+                                         streaming_audio_tower=tower(modules, 4))
+    tails = {}
+    for t in range(4):
+        sids = ["a", "b"] if t < 2 else ["b", "a", "c"]
+        rows = [(s, 0, "e", t if s != "c" else t - 2) for s in sids]
+        pcm = np.zeros((len(sids), 1280), np.float32)
+        batch, states = _listener_batch(f"x{t}", rows, pcm)
+        refs = []
+        for i, (s, _, _, f) in enumerate(rows):
+            ref = None if (s == "b" and t == 1) else synthetic.session_audio(8, ord(s), 1, first_frame=f,
+                                                                              total_frames=4)[0]
+            batch.frames[i].reference_pcm = ref
+            refs.append(np.zeros(1280, np.float32) if ref is None else ref)
+        p = fe.encode_batch(batch, states)
+        want = []
+        for s, ref in zip(sids, refs):
+            m, tails[s] = mel_ref.extract_single_frame(ref, tails.get(s))
+            want.append(m)
+        np.testing.assert_allclose(p.assistant_mels.cpu().numpy(), np.stack(want), rtol=0, atol=2e-4)
+        p.commit()
+    fe.close()
+
+
 def test_frontend_transaction_rules(modules):
     """One active manifest, single owner thread, poisoning after an abort."""
     import threading

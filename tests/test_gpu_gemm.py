@@ -101,15 +101,20 @@ def test_gemm_rejects_bad_strides_and_alignment(lib):
     assert lib.lb_op_gemm(*args(x.data_ptr(), 256, 256, o=192)) == -1   # out_features % 128
     bounds = torch.tensor([-1.0, 1.0])
     rc = lib.lb_op_gemm_clipped(x.data_ptr(), 256, 8, 0, w.data_ptr(), 0, None, None, 256, 128,
-                                out.data_ptr(), 256, 2, 0, 2, 1, bounds.data_ptr(), None, None, s)
-    assert rc == -1  # split-K partial sums cannot be clamped
+                                out.data_ptr(), 256, 2, 0, 2, 1, bounds.data_ptr(), None, None, None, s)
+    assert rc == -1  # atomically accumulated partial sums cannot be clamped
+    rc = lib.lb_op_gemm_clipped(x.data_ptr(), 256, 8, 0, w.data_ptr(), 0, None, None, 256, 128,
+                                out.data_ptr(), 256, 1, 0, 2, 1, bounds.data_ptr(), None, None, None, s)
+    assert rc == -1  # a split-K reduction with a finish pass needs its workspace
     rc = lib.lb_op_gemm_clipped(x.data_ptr(), 128, 8, 4, w.data_ptr(), 0, None, None, 384, 128,
-                                out.data_ptr(), 384, 1, 0, 1, 3, None, None, None, s)
+                                out.data_ptr(), 384, 1, 0, 1, 3, None, None, None, None, s)
     assert rc == -1  # a part's activation block (4 rows apart) shorter than m
 
 
-def run_clipped(lib, M, O, K, int8, mode, act, parts, x_part_rows, seed, bias=True):
-    """lb_op_gemm_clipped vs torch: per-part output clamp, SiLU, next-input clamp."""
+def run_clipped(lib, M, O, K, int8, mode, act, parts, x_part_rows, seed, bias=True, splits=1, calls=1):
+    """lb_op_gemm_clipped vs torch: per-part output clamp, SiLU, next-input clamp;
+    splits > 1 reduces through the workspace and a finish pass (workspace zero
+    on entry, checked zero again after every call)."""
     g = torch.Generator().manual_seed(seed)
     dev = torch.device("cuda")
     dt = torch.float16 if int8 else torch.bfloat16
@@ -143,15 +148,20 @@ def run_clipped(lib, M, O, K, int8, mode, act, parts, x_part_rows, seed, bias=Tr
         hits += int(((yj < float(ob[j, 0])) | (yj > float(ob[j, 1]))).sum())
     if act:
         ref = torch.clamp(torch.nn.functional.silu(ref.to(torch.bfloat16).float()), float(pb[0]), float(pb[1]))
-    out = torch.zeros(M, O, dtype=torch.bfloat16 if mode == 0 else torch.float32, device=dev)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
-    rc = lib.lb_op_gemm_clipped(x.data_ptr(), K, M, x_part_rows, wptr, int8, sptr,
-                                b.data_ptr() if bias else None, O, K, out.data_ptr(), O, mode, act, 1, parts,
-                                ob.reshape(-1).contiguous().data_ptr(),
-                                pb.data_ptr() if pb is not None else None, status.data_ptr(),
-                                torch.cuda.current_stream().cuda_stream)
-    torch.cuda.synchronize()
-    assert rc == 0 and status.item() == 0
+    acc = torch.zeros(M, O, device=dev) if splits > 1 else None
+    for _ in range(calls):
+        out = torch.zeros(M, O, dtype=torch.bfloat16 if mode == 0 else torch.float32, device=dev)
+        rc = lib.lb_op_gemm_clipped(x.data_ptr(), K, M, x_part_rows, wptr, int8, sptr,
+                                    b.data_ptr() if bias else None, O, K, out.data_ptr(), O, mode, act, splits,
+                                    parts, ob.reshape(-1).contiguous().data_ptr(),
+                                    pb.data_ptr() if pb is not None else None,
+                                    acc.data_ptr() if acc is not None else None, status.data_ptr(),
+                                    torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        assert rc == 0 and status.item() == 0
+        if splits > 1:
+            assert acc.abs().max().item() == 0, "workspace not left zero"
     # the bounds must bind somewhere, or the check is vacuous
     assert hits >= max(1, M * O // 1000), hits
     return out.float(), ref
@@ -177,4 +187,24 @@ def test_gemm_stacked_qkv_parts_match_torch(lib, M, int8, x_parts):
     and (x_parts) their own activation blocks (per-projection input clamps)."""
     out, ref = run_clipped(lib, M, 3 * 1536, 1536, int8, 0, 0, 3, M + 64 if x_parts else 0,
                            seed=500 + M + int8)
+    torch.testing.assert_close(out, ref, rtol=1.6e-2, atol=1e-3)
+
+
+@pytest.mark.parametrize("M", [2, 40, 300])
+@pytest.mark.parametrize("int8", [0, 1, 2])
+@pytest.mark.parametrize("mode,act,splits", [(1, 0, 3), (0, 1, 4), (0, 0, 6)])
+def test_gemm_split_k_with_finish_pass_matches_torch(lib, M, int8, mode, act, splits):
+    """K splits reduced through the workspace, the finish pass applying clamps /
+    SiLU; two calls in a row (the workspace is reused)."""
+    out, ref = run_clipped(lib, M, 1536, 3072, int8, mode, act, 1, 0, seed=900 + M + int8 + splits,
+                           splits=splits, calls=2)
+    if mode == 1:
+        torch.testing.assert_close(out, ref, rtol=1e-4, atol=1e-4 * ref.abs().max().item())
+    else:
+        torch.testing.assert_close(out, ref, rtol=1.6e-2, atol=1e-3)
+
+
+@pytest.mark.parametrize("x_parts", [False, True])
+def test_gemm_split_k_stacked_parts_match_torch(lib, x_parts):
+    out, ref = run_clipped(lib, 24, 3 * 1536, 1536, 1, 0, 0, 3, 64 if x_parts else 0, seed=77, splits=3, calls=2)
     torch.testing.assert_close(out, ref, rtol=1.6e-2, atol=1e-3)
