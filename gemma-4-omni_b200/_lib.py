@@ -100,6 +100,7 @@ SIGNATURES: dict[str, tuple] = {
     "lb_debug_read_buffer": (I, [P, ctypes.c_char_p, P, ctypes.c_size_t, P]),
     "lb_get_counters": (I, [P, ctypes.POINTER(LbCounters), P]),
     "lb_mel_async": (I, [P, I, P, P, P, P, P]),
+    "lb_op_control6_head": (I, [I, P, I, P, P, P, P, P, I, ctypes.c_float, P, P, P]),
     "lb_film_talker_async": (I, [P, I, P, I, P, P, P, P, P]),
     "lb_reset_handles_async": (I, [P, I, P, P]),
     "lb_op_gemm": (I, [P, I, I, P, I, P, P, I, I, P, I, I, I, I, P, P]),

@@ -206,6 +206,24 @@ int lb_film_talker_async(lb_ctx* ctx, int n, const void* response_hidden, int ma
                          const int32_t* n_states, const int32_t* steps, const void* query, void* out,
                          void* stream);
 
+/* The batched Control6 policy head over native listener hidden rows: the
+ * tensor part of GemmaNativeControl6BatchPolicy.step_batch
+ * (duplex_kernel/gemma_native_control6_batch_policy.py:853-893) over
+ * NativeControl6LoRA.forward (training/duplex_qlora/native_control6.py:157-197),
+ * one launch for n rows.  hidden bf16 [n][hidden_ld] (the final-normalised
+ * 1536-wide state; hidden_ld >= 1536, e.g. 3072 for the first token of
+ * [n][2][1536]); phase f32 [n][4] or NULL (zeros); legal uint8 [n], bit a =
+ * action a legal, or NULL (all legal); base_rows bf16 [6][1536] (the tied
+ * LM-head rows); lora_a f32 [rank][1540]; lora_b f32 [6][rank]; 1 <= rank <= 64.
+ * logits_out f32 [n][6] = bf16(base_rows . h) + scaling * B(A [h; phase]);
+ * packet_out f32 [n][4] = (all six logits finite, argmax, argmax over the legal
+ * actions, softmax probability of that action among the legal ones); argmax
+ * ties resolve to the lowest action index.  Device pointers; asynchronous. */
+int lb_op_control6_head(int n, const void* hidden, int hidden_ld, const float* phase,
+                        const uint8_t* legal, const void* base_rows, const float* lora_a,
+                        const float* lora_b, int rank, float scaling, float* logits_out,
+                        float* packet_out, void* stream);
+
 /* Synchronous reads (they synchronise the given stream). */
 int lb_get_status(lb_ctx* ctx, int32_t* status_out, void* stream);
 /* Asynchronous: clears the status word, keeping its bits in the history

@@ -26,6 +26,8 @@ Fixtures:
                      epoch change, input masks)
   pcm_tower_nt.npz   PCM -> _extract_single_frame -> StreamingConformerAudioTower
                      (SMALL, non-identity parameters), 3 sessions x 12 ticks
+  control6.npz       NativeControl6LoRA (rank 16) + the batch policy's selection
+                     over 24 seeded rows, with and without phase_t
   film.npz           FrameResidualQueryFiLMAdapter (1536/2048/256 and the SMALL dims),
                      default and non-identity LayerNorm parameters
   packer.npz         slot ids / reasons / committed positions of the tower's slot
@@ -193,6 +195,44 @@ def make_pcm_tower(pkg):
                 frames[s] += 1
     return {"seed_w": 35, "nontrivial": np.bool_(True), "rows": json.dumps(rows_meta),
             "pcm": np.concatenate(pcms), "raw": np.concatenate(raws), "soft": np.concatenate(softs)}
+
+
+def make_control6(pkg):
+    """NativeControl6LoRA.forward on bf16 tied rows + the batch policy's per-row
+    selection (gemma_native_control6_batch_policy.py:878-893) on seeded inputs:
+    ties, restricted and single-action legal sets, phase_t on and off."""
+    from training.duplex_qlora.native_control6 import NativeControl6LoRA
+
+    g = torch.Generator().manual_seed(606)
+    base_rows = (torch.randn(6, 1536, generator=g) * 0.05).to(torch.bfloat16)
+    torch.manual_seed(607)
+    ad = NativeControl6LoRA(base_rows, rank=16, alpha=32.0).eval()
+    with torch.no_grad():
+        ad.lora_B.copy_(torch.randn(6, 16, generator=g) * 0.05)
+    n = 24
+    hidden = torch.randn(n, 1536, generator=g).to(torch.bfloat16)
+    hidden[5] = hidden[4]  # identical rows
+    phase = torch.randn(n, 4, generator=g)
+    legal = torch.rand(n, 6, generator=g) < 0.6
+    legal[0] = True
+    legal[1] = False
+    legal[1, 3] = True  # a single legal action
+    legal[legal.sum(1) == 0, 0] = True
+    out = {}
+    with torch.inference_mode():
+        for tag, ph in (("phase", phase), ("nophase", None)):
+            logits = ad(hidden, phase_t=ph).float()
+            finite = torch.isfinite(logits).all(dim=1).float()
+            raw = logits.argmax(dim=1)
+            selected_logits = logits.masked_fill(~legal, -torch.inf)
+            sel = selected_logits.argmax(dim=1)
+            conf = torch.softmax(selected_logits, dim=1).gather(1, sel.unsqueeze(1)).squeeze(1)
+            out[f"{tag}_logits"] = logits.numpy()
+            out[f"{tag}_packet"] = torch.stack((finite, raw.float(), sel.float(), conf), dim=1).numpy()
+    out.update(hidden=hidden.float().numpy(), phase=phase.numpy(), legal=legal.numpy(),
+               base_rows=base_rows.float().numpy(), lora_a=ad.lora_A.detach().numpy(),
+               lora_b=ad.lora_B.detach().numpy(), scaling=np.float32(ad.scaling))
+    return out
 
 
 def make_mel(pkg):
@@ -416,6 +456,7 @@ def main() -> None:
         "tower_small_nt": lambda: run_tower(pkg, SMALL, 33, 713, "small", nontrivial=True),
         "tower_full_nt": lambda: full_tower(43, 126, "full_nt", nontrivial=True),
         "pcm_tower_nt": lambda: make_pcm_tower(pkg),
+        "control6": lambda: make_control6(pkg),
     }
     unknown = only - set(makers)
     if unknown:

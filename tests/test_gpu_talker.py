@@ -114,3 +114,74 @@ def test_film_talker_is_refused_while_a_step_is_packed(pkg):
     assert rc == -3  # LB_ERR_STATE
     eng.abort()
     eng.close()
+
+
+def _control6(lib, hidden, hidden_ld, phase, legal_bits, base, lora_a, lora_b, scaling):
+    n = hidden.shape[0]
+    logits = torch.empty(n, 6, device="cuda")
+    packet = torch.empty(n, 4, device="cuda")
+    rc = lib.lb_op_control6_head(n, hidden.data_ptr(), hidden_ld, None if phase is None else phase.data_ptr(),
+                                 None if legal_bits is None else legal_bits.data_ptr(), base.data_ptr(),
+                                 lora_a.data_ptr(), lora_b.data_ptr(), lora_a.shape[0], scaling,
+                                 logits.data_ptr(), packet.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    torch.cuda.synchronize()
+    return logits.cpu(), packet.cpu()
+
+
+def _bits(legal: torch.Tensor) -> torch.Tensor:
+    return (legal.to(torch.uint8) << torch.arange(6, dtype=torch.uint8)).sum(1).to(torch.uint8).cuda()
+
+
+def check_selection(logits, packet, ref_logits, ref_packet):
+    # logits: fp32 sums in another order, and the bf16 product of the frozen
+    # rows may round to the neighbouring bf16 value
+    tol = 2 ** -7 * ref_logits.abs() + 1e-5
+    assert bool(((logits - ref_logits).abs() <= tol).all()), (logits - ref_logits).abs().max()
+    assert torch.equal(packet[:, 0], ref_packet[:, 0])
+    # indices are exact unless two logits are within the tolerance of each other
+    for i in range(len(packet)):
+        for col in (1, 2):
+            a, b = int(packet[i, col]), int(ref_packet[i, col])
+            if a != b:
+                assert abs(float(ref_logits[i, a] - ref_logits[i, b])) <= float(tol[i].max()) * 2, (i, col)
+    torch.testing.assert_close(packet[:, 3], ref_packet[:, 3], rtol=1e-3, atol=1e-4)
+
+
+def test_control6_head_matches_reference_golden(pkg):
+    from gemma4_omni_b200 import _lib
+
+    lib = _lib.load()
+    g = np.load(GOLD / "control6.npz")
+    hidden = torch.from_numpy(g["hidden"]).to(torch.bfloat16)
+    # the rows sit as the first token of [n, 2, 1536] listener outputs (row stride 3072)
+    pair = torch.zeros(hidden.shape[0], 2, 1536, dtype=torch.bfloat16)
+    pair[:, 0] = hidden
+    pair[:, 1] = -7.0
+    base = torch.from_numpy(g["base_rows"]).to(torch.bfloat16).cuda()
+    lora_a, lora_b = torch.from_numpy(g["lora_a"]).cuda(), torch.from_numpy(g["lora_b"]).cuda()
+    legal = torch.from_numpy(g["legal"])
+    for tag, phase in (("phase", torch.from_numpy(g["phase"]).cuda()), ("nophase", None)):
+        logits, packet = _control6(lib, pair.cuda(), 3072, phase, _bits(legal), base, lora_a, lora_b,
+                                   float(g["scaling"]))
+        check_selection(logits, packet, torch.from_numpy(g[f"{tag}_logits"]), torch.from_numpy(g[f"{tag}_packet"]))
+
+
+@pytest.mark.parametrize("n,rank", [(1, 16), (300, 16), (4096, 8), (33, 64)])
+def test_control6_head_matches_oracle(pkg, n, rank):
+    from gemma4_omni_b200 import _lib
+    from oracle import control6_ref
+
+    lib = _lib.load()
+    g = torch.Generator().manual_seed(n + rank)
+    hidden = torch.randn(n, 1536, generator=g).to(torch.bfloat16)
+    phase = torch.randn(n, 4, generator=g)
+    legal = torch.rand(n, 6, generator=g) < 0.5
+    legal[legal.sum(1) == 0, 2] = True
+    base = (torch.randn(6, 1536, generator=g) * 0.05).to(torch.bfloat16)
+    lora_a = torch.randn(rank, 1540, generator=g) * 0.02
+    lora_b = torch.randn(6, rank, generator=g) * 0.05
+    ref_logits, ref_packet = control6_ref.control6_head(hidden, phase, legal, base, lora_a, lora_b, 2.0)
+    logits, packet = _control6(lib, hidden.cuda(), 1536, phase.cuda(), _bits(legal), base.cuda(), lora_a.cuda(),
+                               lora_b.cuda(), 2.0)
+    check_selection(logits, packet, ref_logits, ref_packet)

@@ -137,3 +137,18 @@ def test_oracle_coordinator_order_matches_reference():
     reasons = {ev["reason"] for ev in g["events"] if ev["kind"] == "take"}
     assert {"batch_full", "multiple_ready", "coalesce_deadline", None} <= reasons
     assert replay_coordinator(g, packer_ref.order_ready_heads) > 50
+
+
+def test_oracle_control6_head_matches_reference():
+    """The Control6 head restatement vs NativeControl6LoRA + the batch policy's
+    selection (tests/golden/control6.npz)."""
+    from oracle import control6_ref
+
+    g = np.load(GOLD / "control6.npz")
+    args = (torch.from_numpy(g["legal"]), torch.from_numpy(g["base_rows"]).to(torch.bfloat16),
+            torch.from_numpy(g["lora_a"]), torch.from_numpy(g["lora_b"]), float(g["scaling"]))
+    hidden = torch.from_numpy(g["hidden"]).to(torch.bfloat16)
+    for tag, phase in (("phase", torch.from_numpy(g["phase"])), ("nophase", None)):
+        logits, packet = control6_ref.control6_head(hidden, phase, *args)
+        torch.testing.assert_close(logits, torch.from_numpy(g[f"{tag}_logits"]), rtol=1e-5, atol=1e-6)
+        torch.testing.assert_close(packet, torch.from_numpy(g[f"{tag}_packet"]), rtol=1e-5, atol=1e-6)
