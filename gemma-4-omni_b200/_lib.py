@@ -29,6 +29,9 @@ DEV_SLOT_EXHAUSTED = 1 << 1
 DEV_DUPLICATE_ROW = 1 << 2
 DEV_BAD_HANDLE = 1 << 3
 DEV_STALE_COMMIT = 1 << 4
+DEV_BAD_ROW_COUNT = 1 << 5
+DEV_INGRESS_OVERFLOW = 1 << 6
+INGRESS_JOIN, INGRESS_LEAVE, INGRESS_PAUSE, INGRESS_RESUME = 0, 1, 2, 3
 
 
 class LbConfig(ctypes.Structure):
@@ -101,6 +104,12 @@ SIGNATURES: dict[str, tuple] = {
     "lb_get_counters": (I, [P, ctypes.POINTER(LbCounters), P]),
     "lb_mel_async": (I, [P, I, P, P, P, P, P]),
     "lb_op_control6_head": (I, [I, P, I, P, P, P, P, P, I, ctypes.c_float, P, P, P]),
+    "lb_ingress_create": (I, [I, I, I, ctypes.POINTER(P)]),
+    "lb_ingress_destroy": (I, [P]),
+    "lb_ingress_events_async": (I, [P, I, P, P, P, P]),
+    "lb_ingress_push_async": (I, [P, I, P, P, P, P, P]),
+    "lb_ingress_tick_async": (I, [P, I64, P, P, P, P, P, P]),
+    "lb_ingress_get_status": (I, [P, P, P]),
     "lb_film_talker_async": (I, [P, I, P, I, P, P, P, P, P]),
     "lb_reset_handles_async": (I, [P, I, P, P]),
     "lb_op_gemm": (I, [P, I, I, P, I, P, P, I, I, P, I, I, I, I, P, P]),

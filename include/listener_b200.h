@@ -47,7 +47,16 @@ enum lb_device_status_bits {
   LB_DEV_DUPLICATE_ROW = 1 << 2,
   LB_DEV_BAD_HANDLE = 1 << 3,
   LB_DEV_STALE_COMMIT = 1 << 4,
-  LB_DEV_BAD_ROW_COUNT = 1 << 5
+  LB_DEV_BAD_ROW_COUNT = 1 << 5,
+  LB_DEV_INGRESS_OVERFLOW = 1 << 6 /* a frame found its session's ingress ring full (refused) */
+};
+
+/* Session events of the GPU ingress (lb_ingress_events_async). */
+enum lb_ingress_event {
+  LB_INGRESS_JOIN = 0,  /* register (appended to the registration order); arg = directory handle */
+  LB_INGRESS_LEAVE = 1, /* unregister; its queued frames are dropped */
+  LB_INGRESS_PAUSE = 2,
+  LB_INGRESS_RESUME = 3
 };
 
 /* Tensor element types for lb_set_tensor. */
@@ -223,6 +232,41 @@ int lb_op_control6_head(int n, const void* hidden, int hidden_ld, const float* p
                         const uint8_t* legal, const void* base_rows, const float* lora_a,
                         const float* lora_b, int rank, float scaling, float* logits_out,
                         float* packet_out, void* stream);
+
+/* ------------------------------------------------------------------
+ * GPU-resident ingress: the fixed-grid dispatcher's per-session queues and its
+ * row snapshot on the device (SharedListenerTickDispatcher, register_session /
+ * pause / unregister and _snapshot_ready_rows,
+ * duplex_kernel/shared_listener_scheduler.py:80-535).  Every session index
+ * (chosen by the caller, < max_sessions) owns a ring of ring_frames PCM frames
+ * with their frame ids and enqueue times.  Per tick the caller enqueues the
+ * session events, pushes the frames that arrived (one H2D copy of the batch)
+ * and runs the tick, which emits -- in registration order, skipping paused
+ * sessions -- each session's oldest queued frame enqueued no later than the
+ * deadline (a later one stays queued: the reference's deferral), consumes it,
+ * and gathers the rows' PCM into a [max_rows][1280] buffer ready for
+ * lb_step_async.  At most max_rows rows per tick; ready frames past that stay
+ * queued.  The ring is bounded: a push that finds it full is refused with
+ * LB_DEV_INGRESS_OVERFLOW.  Device pointers; asynchronous on `stream`.
+ * ------------------------------------------------------------------ */
+typedef struct lb_ingress lb_ingress;
+int lb_ingress_create(int max_sessions, int ring_frames, int max_rows, lb_ingress** out);
+int lb_ingress_destroy(lb_ingress* ing);
+/* n <= 1024 events applied in order: kind (lb_ingress_event), session index,
+ * arg (the session's directory handle for LB_INGRESS_JOIN).  An index released
+ * by LEAVE must not JOIN again in the same call. */
+int lb_ingress_events_async(lb_ingress* ing, int n, const int32_t* kind, const int32_t* session,
+                            const int32_t* arg, void* stream);
+/* n arrived frames, at most one per session per call: session index, frame
+ * id, enqueue time (ns) and PCM f32 [n][1280] (16-byte aligned). */
+int lb_ingress_push_async(lb_ingress* ing, int n, const int32_t* session, const int64_t* frame_id,
+                          const int64_t* enqueue_ns, const float* pcm, void* stream);
+/* One tick: row_session / row_handle int32 [max_rows], row_frame int64
+ * [max_rows], row_pcm f32 [max_rows][1280], *n_rows (device int32). */
+int lb_ingress_tick_async(lb_ingress* ing, int64_t deadline_ns, int32_t* row_session, int32_t* row_handle,
+                          int64_t* row_frame, float* row_pcm, int32_t* n_rows, void* stream);
+/* Ingress status bits (LB_DEV_*; synchronises `stream`). */
+int lb_ingress_get_status(lb_ingress* ing, int32_t* status_out, void* stream);
 
 /* Synchronous reads (they synchronise the given stream). */
 int lb_get_status(lb_ctx* ctx, int32_t* status_out, void* stream);
