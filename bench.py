@@ -71,6 +71,9 @@ def parse():
     ap.add_argument("--no-sweep", action="store_true", help="skip the real-time capacity sweep")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-small", action="store_true", help="skip the small-N weight-streaming sweep")
+    ap.add_argument("--gemm-probe", type=int, default=0, metavar="M",
+                    help="only time the FFN1 GEMM (1536 -> 6144) at M tokens with the weight kind the step "
+                         "uses there, and report its HBM GB/s (a small case for kernel profiles)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--cpu-sessions", type=int, default=256,
                     help="sessions of the CPU port's bounded sample of the workload")
@@ -494,9 +497,60 @@ def step_roofline_ms(n: int, weights: str, peaks: dict) -> float:
                      (W + n * 1.24e6) / (peaks.get("hbm_gbs", 6650.0) * 1e9))
 
 
+def gemm_probe(args, pkg) -> dict:
+    """The step's FFN1 GEMM alone at M tokens (int8: in-kernel widening below
+    512 tokens, fp16 codes from there), timed with CUDA events on its stream;
+    algorithmic bytes = weights (+ scales) + activations in + outputs out."""
+    import torch
+    from gemma4_omni_b200 import _lib
+    from gemma4_omni_b200.config import FULL
+
+    lib = _lib.load()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    M, O, K = args.gemm_probe, FULL.ffn, FULL.hidden
+    int8 = args.weights == "int8"
+    w_kind = (2 if M >= 512 else 1) if int8 else 0
+    x = torch.randn(M, K, device=dev).to(torch.float16 if int8 else torch.bfloat16)
+    if int8:
+        w = torch.randint(-127, 128, (O, K), dtype=torch.int8, device=dev)
+        if w_kind == 2:
+            w = w.to(torch.float16)
+        sc = torch.full((O,), 1e-3, dtype=torch.float16, device=dev)
+    else:
+        w, sc = (torch.randn(O, K, device=dev) * 0.02).to(torch.bfloat16), None
+    y = torch.empty(M, O, dtype=torch.bfloat16, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    # the step's split count for this shape (SMs filled by K slices)
+    acc = torch.zeros(M, O, device=dev)
+
+    def run(splits):
+        rc = lib.lb_op_gemm_clipped(x.data_ptr(), K, M, 0, w.data_ptr(), w_kind, None if sc is None else sc.data_ptr(),
+                                    None, O, K, y.data_ptr(), O, 0, 1, splits, 1, None, None,
+                                    acc.data_ptr() if splits > 1 else None, None, stream.cuda_stream)
+        assert rc == 0
+    out = {"M": M, "w_kind": w_kind, "per_splits": {}}
+    for splits in (1, 3):
+        for _ in range(5):
+            run(splits)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(50):
+            run(splits)
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        us = a.elapsed_time(b) / 50 * 1e3
+        nbytes = w.numel() * w.element_size() + (O * 2 if int8 else 0) + x.numel() * 2 + y.numel() * 2
+        out["per_splits"][str(splits)] = {"us": us, "algorithmic_bytes": nbytes, "achieved_gbs": nbytes / us / 1e3}
+    return out
+
+
 def main():
     args = parse()
     pkg = load_package()
+    if args.gemm_probe:
+        print(json.dumps({"gemm_probe": gemm_probe(args, pkg)}), flush=True)
+        return
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))

@@ -481,7 +481,7 @@ int make_op(Ctx& c, GemmOp& op, void* w, const __half* scale, int O, int K, cons
 // partial-sum buffer is zero at creation and after every finish pass.
 cudaError_t run_op(Ctx& c, const GemmOp& op, int tok_cap, cudaStream_t s) {
   cudaError_t e = gemm_launch(op.plan, op.params, op.splits, s, op.pdl);
-  if (e != cudaSuccess || op.splits <= 1) return e;
+  if (e != cudaSuccess || op.splits <= 1 || op.consumer_finishes) return e;
   FinalizeClip fc;
   fc.part_o = op.params.part_o;
   for (int j = 0; j < 3; ++j) {
@@ -514,12 +514,15 @@ int build_plans(lb_ctx* x, int bi) {
       GemmOp& a2 = f == 0 ? o.ffn1[1] : o.ffn2[1];
       rc |= make_op(c, a1, L.w_ffn1[f], L.s_ffn1[f], F, d, c.xa, tc, nullptr, c.xf, 2, 1, c1, c2[0], c2[1]);
       rc |= make_op(c, a2, L.w_ffn2[f], L.s_ffn2[f], d, F, c.xf, tc, nullptr, c.y, 1, 0, c2);
+      a2.consumer_finishes = true;
     }
     rc |= make_op(c, o.qkv, L.w_qkv, L.s_qkv, 3 * d, d, c.xa, tc, nullptr, c.qkv, 0, 0, L.clip[kLinQkv],
                   -INFINITY, INFINITY, &L);
     rc |= make_op(c, o.post, L.w_post, L.s_post, d, d, c.att, tc, nullptr, c.y, 1, 0, L.clip[kLinPost]);
+    o.post.consumer_finishes = true;
     rc |= make_op(c, o.lstart, L.w_lstart, L.s_lstart, 2 * d, d, c.xa, tc, nullptr, c.gl, 0, 0, L.clip[kLinStart]);
     rc |= make_op(c, o.lend, L.w_lend, L.s_lend, d, d, c.xa, tc, nullptr, c.y, 1, 0, L.clip[kLinEnd]);
+    o.lend.consumer_finishes = true;
   }
   rc |= make_op(c, P.out_proj, c.w.w_out, c.w.s_out, g.output_dims, d, c.xa, tc, c.w.b_out, c.y, 1, 0, nullptr);
   rc |= make_op(c, P.embed, c.w.w_embed, c.w.s_embed, g.text_hidden, g.output_dims, c.xe, tc, nullptr, c.y, 1, 0, nullptr);
@@ -534,6 +537,19 @@ int build_plans(lb_ctx* x, int bi) {
   if (rc) return LB_ERR_CUDA;
   P.built = true;
   return 0;
+}
+
+// The row kernel after an op that writes y: from y itself, or from the
+// split-K partial sums, which it then finishes (output clamp) and re-zeroes.
+void bind_y(Ctx& c, const GemmOp& op, RowFusedArgs& r) {
+  if (op.splits > 1 && op.consumer_finishes) {
+    r.y = c.wide_acc;
+    r.zero_y = true;
+    r.y_lo = op.params.out_lo;
+    r.y_hi = op.params.out_hi;
+  } else {
+    r.y = c.y;
+  }
 }
 
 // Diagnostics only (eager runs): return after stage `k` of layer `i`.
@@ -578,7 +594,7 @@ cudaError_t run_tower(lb_ctx* x, int bi, int input_kind, cudaStream_t s) {
     LB_STOP(i, 1);
     {
       RowFusedArgs r;
-      r.y = c.y;
+      bind_y(c, o.ffn1[1], r);
       r.post_w = L.ffn_post[0];
       r.alpha = g.residual_weight;
       r.pre_w = L.norm_pre_attn;
@@ -604,7 +620,7 @@ cudaError_t run_tower(lb_ctx* x, int bi, int input_kind, cudaStream_t s) {
     LB_STOP(i, 5);
     {
       RowFusedArgs r;
-      r.y = c.y;
+      bind_y(c, o.post, r);
       r.post_w = L.norm_post_attn;
       r.pre_w = L.lc_pre;
       r.pre_clamp = false;
@@ -623,7 +639,7 @@ cudaError_t run_tower(lb_ctx* x, int bi, int input_kind, cudaStream_t s) {
     LB_STOP(i, 9);
     {
       RowFusedArgs r;
-      r.y = c.y;
+      bind_y(c, o.lend, r);
       r.pre_w = L.ffn_pre[1];
       r.in_lo = L.clip[kLinFfn2a][0];
       r.in_hi = L.clip[kLinFfn2a][1];
@@ -638,7 +654,7 @@ cudaError_t run_tower(lb_ctx* x, int bi, int input_kind, cudaStream_t s) {
     LB_STOP(i, 12);
     {
       RowFusedArgs r;
-      r.y = c.y;
+      bind_y(c, o.ffn2[1], r);
       r.post_w = L.ffn_post[1];
       r.alpha = g.residual_weight;
       r.out_w = L.norm_out;

@@ -122,6 +122,10 @@ struct RowFusedDev {
   int xa_parts;
   size_t xa_part_stride;
   float part_lo[2], part_hi[2];
+  // y is a split-K GEMM's partial-sum buffer: finish it here (the linear's
+  // output clamp y_lo / y_hi) and zero it behind the read
+  int zero_y;
+  float y_lo, y_hi;
 };
 
 // One warp per token: lane owns G groups of 8 elements, e = (g*32 + lane)*8,
@@ -146,6 +150,15 @@ __global__ void __launch_bounds__(128, 4) row_fused_kernel(RowFusedDev a) {
     if (a.y) load8(a.y + base + g * 256, y[g]);
   }
   if (t >= n_tok) return;
+  if (a.zero_y) {
+    const float z[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      store8(const_cast<float*>(a.y) + base + g * 256, z);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) y[g][i] = fminf(fmaxf(y[g][i], a.y_lo), a.y_hi);
+    }
+  }
   if (a.y) {
     if (a.post_w) {
       float ss = 0.f;
@@ -496,6 +509,9 @@ cudaError_t launch_row_fused(Ctx& c, int tok_cap, const RowFusedArgs& r, cudaStr
   a.xa = r.xa;
   a.dbg = r.dbg;
   a.f16 = c.f16_acts != 0;
+  a.zero_y = r.zero_y ? 1 : 0;
+  a.y_lo = r.y_lo;
+  a.y_hi = r.y_hi;
   a.xa_parts = r.xa_parts;
   a.xa_part_stride = static_cast<size_t>(2) * c.cfg.max_rows * c.cfg.hidden;
   for (int j = 0; j < 2; ++j) {

@@ -128,6 +128,7 @@ struct GemmOp {
   bool pdl = false;        // launched with programmatic stream serialisation
   int out_kind = 0;        // 0: bf16 / fp16 tensor, 1: fp32 (the split-K finish pass's store)
   void* out = nullptr;     // the op's output (a split-K GEMM itself writes wide_acc)
+  bool consumer_finishes = false;  // split-K: the row kernel after it reads wide_acc and finishes it
 };
 
 struct Bucket {
@@ -277,6 +278,10 @@ struct RowFusedArgs {
   // part_lo/part_hi (the K and V input bounds); block 0 gets in_lo/in_hi
   int xa_parts = 1;
   float part_lo[2] = {-INFINITY, -INFINITY}, part_hi[2] = {INFINITY, INFINITY};
+  // y is the split-K partial-sum buffer of the GEMM before: clamp it to the
+  // linear's output bounds and zero it after reading (its finish pass)
+  bool zero_y = false;
+  float y_lo = -INFINITY, y_hi = INFINITY;
 };
 cudaError_t launch_row_fused(Ctx& c, int tok_cap, const RowFusedArgs& a, cudaStream_t s);
 cudaError_t launch_attention(Ctx& c, int layer, int rows_cap, cudaStream_t s);
