@@ -123,3 +123,31 @@ def test_config_validation_rejects_unsupported_shapes(pkg):
         ListenerConfig(hidden=1000).validate()
     with pytest.raises(ValueError):
         ListenerConfig(conv_kernel=3).validate()
+
+
+def test_nontrivial_weights_cover_every_identity_parameter(pkg):
+    """The parity weight set: norm weights != 1, per_dim_scale != 0, biases != 0,
+    finite and distinct q/k/v clip bounds on every clippable linear, and every
+    value exactly representable in bf16 (a bf16 checkpoint)."""
+    import numpy as np
+    import torch
+    from gemma4_omni_b200 import synthetic
+    from gemma4_omni_b200.config import SMALL
+
+    w = synthetic.synthetic_tower_weights(SMALL, 9, nontrivial=True)
+    base = synthetic.synthetic_tower_weights(SMALL, 9)
+    for name, shape, init in synthetic.tower_weight_shapes(SMALL):
+        if init == "normal":  # the default draws are kept (then rounded to bf16)
+            np.testing.assert_allclose(w[name], base[name], rtol=2 ** -8, atol=0)
+        else:
+            assert not np.array_equal(w[name], base[name]), name
+    for prefix, _ in synthetic.clippable_linears(SMALL):
+        b = [float(w[f"{prefix}.{k}"]) for k in ("input_min", "input_max", "output_min", "output_max")]
+        assert all(np.isfinite(b)) and b[0] < 0 < b[1] and b[2] < 0 < b[3], prefix
+    qb = [float(w[f"layers.0.self_attn.{p}.input_max"]) for p in ("q_proj", "k_proj", "v_proj")]
+    assert len(set(qb)) == 3
+    for k, v in w.items():
+        t = torch.from_numpy(np.array(v, dtype=np.float32))
+        assert torch.equal(t.to(torch.bfloat16).float(), t), k
+    f = synthetic.synthetic_film_weights(SMALL, 9, nontrivial=True)
+    assert not np.allclose(f["query_norm.bias"], 0) and not np.allclose(f["response_norm.weight"], 1)
