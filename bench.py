@@ -60,6 +60,45 @@ def load_package():
     return mod
 
 
+def wide_min_tokens() -> int:
+    """Smallest token bucket whose int8 GEMMs read the fp16-widened codes (the
+    library's default, or LB_WIDE_MIN_TOKENS as the library reads it)."""
+    return max(0, int(os.environ.get("LB_WIDE_MIN_TOKENS", "128")))
+
+
+def token_tile(O: int, m: int, sms: int = 148) -> int:
+    """The GEMM's token tile for an [m x O] output (csrc/gemm_tc.cu gemm_token_tile)."""
+    for cap in (32, 64, 128, 256):
+        if m <= cap:
+            return cap
+    best, best_cost = 256, None
+    for tn in (256, 240, 224, 208, 192, 176, 160, 144, 128):
+        units = (O // 128) * -(-m // tn)
+        cost = -(-units // sms) * (tn + 32)
+        if best_cost is None or cost < best_cost:
+            best, best_cost = tn, cost
+    return best
+
+
+def step_splits(O: int, K: int, m: int, sms: int = 148) -> int:
+    """K slices the listener step gives an [m x O x K] GEMM (csrc/gemm_tc.cu
+    gemm_pick_splits and the step's rule in make_op: split only while the tiles
+    fill fewer than half of the SMs)."""
+    tiles = (O // 128) * -(-m // token_tile(O, m, sms))
+    if tiles * 2 >= sms:
+        return 1
+    total_kb = K // 64
+    best, best_eff = 1, tiles / (-(-tiles // sms) * sms)
+    for s in range(2, 17):
+        if total_kb // s < 6:
+            break
+        units = tiles * s
+        eff = units / (-(-units // sms) * sms)
+        if eff > best_eff + 0.08:
+            best, best_eff = s, eff
+    return best
+
+
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -401,12 +440,14 @@ def run_ours(args, pkg, rank, world, device):
     e2e_lat, e2e_value, h2d, d2h = e2e_run(n, args.e2e_steps, 1000 + rank, pool, list(q_pool))
 
     # ---- dominant kernel: the FFN1 GEMM at this step's token count, timed alone,
-    # with the weight kind the step's bucket uses: int8 codes read as fp16-widened
-    # codes from 512 tokens on (w_kind 2), in-kernel widening below (w_kind 1)
+    # with the weight kind and K split the step's bucket uses: int8 codes read as
+    # fp16-widened codes from wide_min_tokens() tokens on (w_kind 2), in-kernel
+    # widening below (w_kind 1)
     M = 2 * n
     w_kind = fmt
-    if fmt == 1 and M >= 512 and os.environ.get("LB_INT8_WIDE", "1") != "0":
+    if fmt == 1 and M >= wide_min_tokens() and os.environ.get("LB_INT8_WIDE", "1") != "0":
         w_kind = 2
+    splits = step_splits(FULL.ffn, FULL.hidden, M)
     x = torch.randn(M, FULL.hidden, device=device).to(torch.float16 if fmt == 1 else torch.bfloat16)
     if fmt == 1:
         wq = torch.randint(-127, 128, (FULL.ffn, FULL.hidden), dtype=torch.int8, device=device)
@@ -417,11 +458,15 @@ def run_ours(args, pkg, rank, world, device):
         wq = (torch.randn(FULL.ffn, FULL.hidden, device=device) * 0.02).to(torch.bfloat16)
         sc_ = None
     yo = torch.empty(M, FULL.ffn, dtype=torch.bfloat16, device=device)
+    # a split GEMM reduces through this zeroed workspace and a finish pass
+    acc_ = torch.zeros(M, FULL.ffn, device=device) if splits > 1 else None
 
     def gemm():
-        return eng.lib.lb_op_gemm(x.data_ptr(), FULL.hidden, M, wq.data_ptr(), w_kind,
-                                  None if sc_ is None else sc_.data_ptr(), None, FULL.ffn, FULL.hidden,
-                                  yo.data_ptr(), FULL.ffn, 0, 1, 1, None, stream.cuda_stream)
+        rc = eng.lib.lb_op_gemm_clipped(x.data_ptr(), FULL.hidden, M, 0, wq.data_ptr(), w_kind,
+                                        None if sc_ is None else sc_.data_ptr(), None, FULL.ffn, FULL.hidden,
+                                        yo.data_ptr(), FULL.ffn, 0, 1, splits, 1, None, None,
+                                        None if acc_ is None else acc_.data_ptr(), None, stream.cuda_stream)
+        assert rc == 0, rc
     for _ in range(5):
         gemm()
     g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -432,7 +477,7 @@ def run_ours(args, pkg, rank, world, device):
     g1.record(stream)
     torch.cuda.synchronize(device)
     gemm_ms = g0.elapsed_time(g1) / reps
-    del x, wq, yo
+    del x, wq, yo, acc_
 
     # ---- weight-streaming regime: small N, device-resident, step time vs the
     # step's algorithmic bytes (weights + per-session state)
@@ -486,7 +531,7 @@ def run_ours(args, pkg, rank, world, device):
     eng.close()
     return dict(elapsed_ms=elapsed_ms, lat=lat, frames=frames, kernels=kernels_per_step,
                 clocks=clk.summary(), e2e_value=e2e_value, e2e_lat=e2e_lat, h2d=h2d, d2h=d2h, gemm_ms=gemm_ms, M=M,
-                w_kind=w_kind, sweep=sweep_res, small=small, c4=c4, eff=eff)
+                w_kind=w_kind, gemm_splits=splits, sweep=sweep_res, small=small, c4=c4, eff=eff)
 
 
 def step_roofline_ms(n: int, weights: str, peaks: dict) -> float:
@@ -499,7 +544,8 @@ def step_roofline_ms(n: int, weights: str, peaks: dict) -> float:
 
 def gemm_probe(args, pkg) -> dict:
     """The step's FFN1 GEMM alone at M tokens (int8: in-kernel widening below
-    512 tokens, fp16 codes from there), timed with CUDA events on its stream;
+    wide_min_tokens(), fp16 codes from there) with 1 and 3 K slices (3: through
+    a workspace and a finish pass), timed with CUDA events on its stream;
     algorithmic bytes = weights (+ scales) + activations in + outputs out."""
     import torch
     from gemma4_omni_b200 import _lib
@@ -510,7 +556,7 @@ def gemm_probe(args, pkg) -> dict:
     torch.cuda.set_device(dev)
     M, O, K = args.gemm_probe, FULL.ffn, FULL.hidden
     int8 = args.weights == "int8"
-    w_kind = (2 if M >= 512 else 1) if int8 else 0
+    w_kind = (2 if M >= wide_min_tokens() else 1) if int8 else 0
     x = torch.randn(M, K, device=dev).to(torch.float16 if int8 else torch.bfloat16)
     if int8:
         w = torch.randint(-127, 128, (O, K), dtype=torch.int8, device=dev)
@@ -616,7 +662,16 @@ def main():
     ms_step = elapsed_ms / args.steps
     M = res["M"]
     gemm_flops = 2.0 * M * FULL.ffn * FULL.hidden
-    achieved = gemm_flops / (res["gemm_ms"] * 1e-3) / 1e12
+    # algorithmic bytes of the launch: weights (int8 codes, or their fp16
+    # widening) + fp16 scales + fp16 activations in + bf16 outputs
+    w_bytes = FULL.ffn * FULL.hidden * (2 if res["w_kind"] != 1 else 1)
+    gemm_bytes = w_bytes + 2 * FULL.ffn + 2 * M * FULL.hidden + 2 * M * FULL.ffn
+    # the roof that binds this shape: tensor throughput or the weight stream
+    tensor_bound = gemm_flops / (peak_tf * 1e12) >= gemm_bytes / (hbm * 1e9)
+    if tensor_bound:
+        achieved = gemm_flops / (res["gemm_ms"] * 1e-3) / 1e12
+    else:
+        achieved = gemm_bytes / (res["gemm_ms"] * 1e-3) / 1e9
     # DRAM bytes (read + write) of one launch of this GEMM from an ncu --set full
     # capture of the same shape and weight kind (M=2048, fp16 activations): W and
     # X are read once; the 25 MB output stays in L2 by kernel end.
@@ -632,11 +687,17 @@ def main():
         "data": "synthetic (seeded PCM, N(0,0.02) weights, geometric session arrivals)",
         "config": workload_config(args, world),
         "latency_ms": {"p50": p50, "p99": p99, "max": lat[-1], "steps": len(lat), "path": "device-resident"},
-        "roofline": {"bound": "tensor", "kernel": f"FFN1 GEMM {M}x{FULL.ffn}x{FULL.hidden}, weights "
-                     + {0: "bf16", 1: "int8 (widened in-kernel)", 2: "int8 codes widened to fp16"}[res["w_kind"]],
-                     "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s", "frac": achieved / peak_tf,
+        "roofline": {"bound": "tensor" if tensor_bound else "hbm",
+                     "kernel": f"FFN1 GEMM {M}x{FULL.ffn}x{FULL.hidden}, weights "
+                     + {0: "bf16", 1: "int8 (widened in-kernel)", 2: "int8 codes widened to fp16"}[res["w_kind"]]
+                     + (f", {res['gemm_splits']} K slices" if res["gemm_splits"] > 1 else ""),
+                     "achieved": achieved, "peak": peak_tf if tensor_bound else hbm,
+                     "unit": "TFLOP/s" if tensor_bound else "GB/s",
+                     "frac": achieved / (peak_tf if tensor_bound else hbm),
+                     "algorithmic": gemm_flops if tensor_bound else gemm_bytes,
                      "traffic": traffic, "traffic_source": traffic_src,
-                     "peak_source": f"{peak_src} bf16 burst (kernel timed alone)"},
+                     "peak_source": (f"{peak_src} bf16 burst (kernel timed alone)" if tensor_bound
+                                     else f"{peak_src} HBM copy bandwidth")},
         "roofline_step": {"t_roof_ms": t_roof, "t_measured_ms": ms_step, "frac": t_roof / ms_step,
                           "definition": "max(N*2.644 GFLOP / sustained bf16 peak, (W + N*1.24 MB) / HBM peak)"},
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": res["h2d"], "d2h_bytes_per_step": res["d2h"],

@@ -395,23 +395,19 @@ size_t layout_acts(Ctx& c, char* base) {
 }
 
 // ------------------------------------------------------------- GEMM plans
-// Smallest bucket (tokens) whose int8-weight GEMMs read fp16-widened codes:
-// from here on the step is tensor-bound, and the in-kernel widening costs more
-// than the extra weight bytes.
-constexpr int kWideMinTokens = 512;
-
 int make_op(Ctx& c, GemmOp& op, void* w, const __half* scale, int O, int K, const void* x, int tok_cap,
             const float* bias, void* out, int out_kind, int act, const float* clip4,
-            float post_lo = -INFINITY, float post_hi = INFINITY, const LayerW* qkv = nullptr) {
+            float post_lo = -INFINITY, float post_hi = INFINITY, const LayerW* qkv = nullptr,
+            bool consumer_finishes = false) {
   // out_kind: 0 = bf16 tensor, 1 = fp32, 2 = activation that feeds another GEMM
   // (bf16, or fp16 when the weights are int8)
   op.final_f16 = out_kind == 2 && c.f16_acts;
-  // int8 weights: buckets of >= kWideMinTokens tokens read the fp16 codes
+  // int8 weights: buckets of >= wide_min_tokens tokens read the fp16 codes
   // bf16 weights: every bucket reads their exact fp16 copy (same offsets), no scale
   int w_kind = 0;
   if (c.weight_int8) {
     w_kind = 1;
-    if (c.wide_arena && tok_cap >= kWideMinTokens) {
+    if (c.wide_arena && tok_cap >= c.wide_min_tokens) {
       w_kind = 2;
       w = static_cast<char*>(c.wide_arena) +
           2 * (static_cast<char*>(w) - static_cast<char*>(c.weight_arena));
@@ -462,9 +458,12 @@ int make_op(Ctx& c, GemmOp& op, void* w, const __half* scale, int O, int K, cons
   if (tiles * 2 >= c.num_sms || O > c.wide_width) op.splits = 1;
   op.out_kind = out_kind;
   op.out = out;
+  op.consumer_finishes = false;
   if (op.splits > 1) {
     // K slices reduce-add into the context's partial-sum buffer (kept zero:
     // every finish pass zeroes what it read), then the finish pass (run_op)
+    // or the consuming row kernel
+    op.consumer_finishes = consumer_finishes;
     p.out_mode = 2;
     p.out = c.wide_acc;
     p.ld_out = O;
@@ -513,16 +512,16 @@ int build_plans(lb_ctx* x, int bi) {
       GemmOp& a1 = f == 0 ? o.ffn1[0] : o.ffn2[0];
       GemmOp& a2 = f == 0 ? o.ffn1[1] : o.ffn2[1];
       rc |= make_op(c, a1, L.w_ffn1[f], L.s_ffn1[f], F, d, c.xa, tc, nullptr, c.xf, 2, 1, c1, c2[0], c2[1]);
-      rc |= make_op(c, a2, L.w_ffn2[f], L.s_ffn2[f], d, F, c.xf, tc, nullptr, c.y, 1, 0, c2);
-      a2.consumer_finishes = true;
+      rc |= make_op(c, a2, L.w_ffn2[f], L.s_ffn2[f], d, F, c.xf, tc, nullptr, c.y, 1, 0, c2, -INFINITY, INFINITY,
+                    nullptr, true);
     }
     rc |= make_op(c, o.qkv, L.w_qkv, L.s_qkv, 3 * d, d, c.xa, tc, nullptr, c.qkv, 0, 0, L.clip[kLinQkv],
                   -INFINITY, INFINITY, &L);
-    rc |= make_op(c, o.post, L.w_post, L.s_post, d, d, c.att, tc, nullptr, c.y, 1, 0, L.clip[kLinPost]);
-    o.post.consumer_finishes = true;
+    rc |= make_op(c, o.post, L.w_post, L.s_post, d, d, c.att, tc, nullptr, c.y, 1, 0, L.clip[kLinPost], -INFINITY,
+                  INFINITY, nullptr, true);
     rc |= make_op(c, o.lstart, L.w_lstart, L.s_lstart, 2 * d, d, c.xa, tc, nullptr, c.gl, 0, 0, L.clip[kLinStart]);
-    rc |= make_op(c, o.lend, L.w_lend, L.s_lend, d, d, c.xa, tc, nullptr, c.y, 1, 0, L.clip[kLinEnd]);
-    o.lend.consumer_finishes = true;
+    rc |= make_op(c, o.lend, L.w_lend, L.s_lend, d, d, c.xa, tc, nullptr, c.y, 1, 0, L.clip[kLinEnd], -INFINITY,
+                  INFINITY, nullptr, true);
   }
   rc |= make_op(c, P.out_proj, c.w.w_out, c.w.s_out, g.output_dims, d, c.xa, tc, c.w.b_out, c.y, 1, 0, nullptr);
   rc |= make_op(c, P.embed, c.w.w_embed, c.w.s_embed, g.text_hidden, g.output_dims, c.xe, tc, nullptr, c.y, 1, 0, nullptr);
@@ -751,6 +750,8 @@ int lb_create(const lb_config* cfg, lb_ctx** out_ctx) {
     const int mode = pdl_env ? std::atoi(pdl_env) : 1;
     c.pdl = mode >= 1;
     c.pdl_all = mode >= 2;
+    const char* wide_env = std::getenv("LB_WIDE_MIN_TOKENS");
+    if (wide_env) c.wide_min_tokens = std::max(0, std::atoi(wide_env));
   }
   c.max_handles = cfg->max_handles;
   if (cudaGetDevice(&c.device) != cudaSuccess) return LB_ERR_CUDA;
@@ -968,7 +969,7 @@ int lb_finalize_weights(lb_ctx* x) {
   if (attention_prepare(c, nullptr) != cudaSuccess || cudaStreamSynchronize(nullptr) != cudaSuccess)
     return LB_ERR_CUDA;
   const char* env = std::getenv("LB_INT8_WIDE");
-  if (c.weight_int8 && 2 * c.cfg.max_rows >= kWideMinTokens && !(env && env[0] == '0')) {
+  if (c.weight_int8 && 2 * c.cfg.max_rows >= c.wide_min_tokens && !(env && env[0] == '0')) {
     {
       cudaSetDevice(c.device);
       const size_t n = c.weight_bytes & ~static_cast<size_t>(15);

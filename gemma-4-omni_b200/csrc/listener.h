@@ -4,9 +4,9 @@
 //
 //   weights   one arena; GEMM weights bf16 [O,K] or int8 [O,K] + fp16 scale[O];
 //             norms / conv / biases fp32 (bf16-rounded values).  With int8
-//             weights and buckets of >= 512 tokens, a second arena holds the
-//             int8 codes widened to fp16 (exact): those GEMMs are tensor-bound,
-//             and fp16 codes skip the in-kernel widening.
+//             weights and buckets of >= 128 tokens, a second arena holds the
+//             int8 codes widened to fp16 (exact): from there on the in-kernel
+//             widening costs more than the extra weight bytes.
 //   sessions  persistent per-slot state, S = max_sessions slots:
 //               kv_k, kv_v  bf16 [L][S][16][d] (+pad per slot, ring_base) ring of the
 //                           last 13 projected keys / values (pre-scale, exactly
@@ -154,6 +154,10 @@ struct Ctx {
   // early too.  LB_PDL=0 / 1 / 2: off / GEMMs only / all kernels.
   bool pdl = true;
   bool pdl_all = false;
+  // int8 weights: buckets of at least this many tokens read the fp16-widened
+  // codes (kept resident beside the int8 arena), smaller ones widen the int8
+  // codes inside the GEMM.  LB_WIDE_MIN_TOKENS overrides it.
+  int wide_min_tokens = 128;
 
   // arenas
   void* weight_arena = nullptr;
