@@ -61,11 +61,13 @@ struct GemmCfg {
   // which caps it at 96 registers per thread, so it drains 16 columns at a time
   static constexpr int kCols = WK == kWInt8 ? 16 : 32;
   static constexpr uint32_t kBBytes = TN * kBlockK * 2;
-  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  // int8 codes land in their own buffer beside the fp16 tile they widen into
+  static constexpr uint32_t kRawStage = WK == kWInt8 ? kRawBytes : 0;
+  static constexpr uint32_t kStageBytes = kABytes + kRawStage + kBBytes;
   // operand ring within 224 KB (the 227 KB opt-in limit leaves room for the
   // barriers and the 1 KB alignment slack)
   static constexpr int kStages = (224 * 1024) / kStageBytes > 8 ? 8 : (224 * 1024) / kStageBytes;
-  static constexpr uint32_t kBarBytes = (5 * kStages + 4) * 8 + 16;
+  static constexpr uint32_t kBarBytes = (4 * kStages + 4) * 8 + 16;
   static constexpr uint32_t kSmemBytes = kStages * kStageBytes + kBarBytes + 1024;
   static constexpr int kThreads = WK == kWInt8 ? 576 : 320;
   // double-buffered accumulator: two power-of-two column blocks of >= TN
@@ -204,18 +206,17 @@ __global__ void __launch_bounds__(GemmCfg<TN, WK>::kThreads, 1)
   const int units = o_tiles * t_tiles * splits;
 
   auto stage_a = [&](int s) { return smem + s * Cfg::kStageBytes; };
-  auto stage_b = [&](int s) { return smem + s * Cfg::kStageBytes + kABytes; };
-  // int8 weights land in the upper half of their stage's fp16 A tile
-  auto stage_raw = [&](int s) { return smem + s * Cfg::kStageBytes + kRawBytes; };
+  auto stage_b = [&](int s) { return smem + s * Cfg::kStageBytes + kABytes + Cfg::kRawStage; };
+  // int8 weights land in the raw buffer after their stage's fp16 A tile
+  auto stage_raw = [&](int s) { return smem + s * Cfg::kStageBytes + kABytes; };
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
   uint64_t* full = bars;                    // bf16: W and X tiles; int8: X tile
   uint64_t* empty = bars + S;
   uint64_t* conv = bars + 2 * S;            // int8: W tile widened to fp16
-  uint64_t* rawrd = bars + 3 * S;           // int8: every converter warp has read the raw tile
-  uint64_t* full_w = bars + 4 * S;          // int8: raw W tile landed
-  uint64_t* tmem_full = bars + 5 * S;       // [2]
-  uint64_t* tmem_empty = bars + 5 * S + 2;  // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 5 * S + 4);
+  uint64_t* full_w = bars + 3 * S;          // int8: raw W tile landed
+  uint64_t* tmem_full = bars + 4 * S;       // [2]
+  uint64_t* tmem_empty = bars + 4 * S + 2;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4 * S + 4);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -226,7 +227,6 @@ __global__ void __launch_bounds__(GemmCfg<TN, WK>::kThreads, 1)
       mbar_init(&empty[s], 1);
       if (WINT8) {
         mbar_init(&conv[s], 8);
-        mbar_init(&rawrd[s], 8);
         mbar_init(&full_w[s], 1);
       }
     }
@@ -446,46 +446,33 @@ __global__ void __launch_bounds__(GemmCfg<TN, WK>::kThreads, 1)
     }
   } else {
     // ---------------- int8 -> fp16 converters (WINT8 only; warps 10..17)
-    // The int8 tile sits in the upper half of the fp16 tile it widens into, so
-    // every converter warp reads its raw chunks and meets the others on
-    // rawrd[s] before anyone writes.  Software-pipelined one stage ahead: the
-    // raw chunks of stage it+1 are read (and rawrd arrived) before stage it is
-    // widened, so the rawrd meeting of stage it is normally already complete.
+    // The raw int8 tile has its own buffer, so each converter warp widens its
+    // rows (8 + 8 of the 128) as soon as the tile lands, with no meeting of the
+    // warps: read 2 x 16 codes, widen, store 4 x 16 bytes into the swizzled
+    // fp16 tile, one proxy fence, one arrival on conv[s] per warp.
     if (WINT8) {
       const int ct = threadIdx.x - 320;
       int n_it = 0;  // k-blocks this CTA streams, in ring order
       for (int u = blockIdx.x; u < units; u += gridDim.x)
         n_it += unit_of(u, o_tiles, t_tiles, TN, p.kb_per_split, total_kb).nkb;
-      auto read_raw = [&](int s, int4 (&r)[2]) {
+      for (int it = 0; it < n_it; ++it) {
+        const int s = it % S;
+        if (!mbar_wait(&full_w[s], (it / S) & 1, p.status)) break;
         const uint8_t* raw = stage_raw(s);
+        uint8_t* dst = stage_a(s);
+        int4 r[2];
 #pragma unroll
         for (int qd = 0; qd < 2; ++qd) {
           const int cidx = ct + 256 * qd;  // 16-byte chunk id in the 128 x 64 B raw tile
           r[qd] = *reinterpret_cast<const int4*>(raw + (cidx >> 2) * 64 + (cidx & 3) * 16);
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&rawrd[s]);
-      };
-      int4 cur[2], nxt[2];
-      bool ok = n_it > 0 && mbar_wait(&full_w[0], 0, p.status);
-      if (ok) read_raw(0, cur);
-      for (int it = 0; ok && it < n_it; ++it) {
-        const int s = it % S;
-        const uint32_t ph = (it / S) & 1;
-        if (it + 1 < n_it) {
-          const int s1 = (it + 1) % S;
-          if (!mbar_wait(&full_w[s1], ((it + 1) / S) & 1, p.status)) break;
-          read_raw(s1, nxt);
-        }
-        if (!mbar_wait(&rawrd[s], ph, p.status)) break;
-        uint8_t* dst = stage_a(s);
 #pragma unroll
         for (int qd = 0; qd < 2; ++qd) {
           const int cidx = ct + 256 * qd;
           const int row = cidx >> 2;
           const int ch = cidx & 3;
           int4 lo4, hi4;
-          convert_i8x16_to_f16(cur[qd], lo4, hi4);
+          convert_i8x16_to_f16(r[qd], lo4, hi4);
           const int sw = row & 7;
           *reinterpret_cast<int4*>(dst + row * 128 + (((2 * ch) ^ sw) << 4)) = lo4;
           *reinterpret_cast<int4*>(dst + row * 128 + (((2 * ch + 1) ^ sw) << 4)) = hi4;
@@ -493,8 +480,6 @@ __global__ void __launch_bounds__(GemmCfg<TN, WK>::kThreads, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&conv[s]);
-        cur[0] = nxt[0];
-        cur[1] = nxt[1];
       }
     }
   }
