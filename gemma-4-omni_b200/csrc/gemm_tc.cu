@@ -254,6 +254,19 @@ __global__ void __launch_bounds__(GemmCfg<TN, WK>::kThreads, 1)
     // ---------------- TMA producer
     if (lane == 0) {
       const uint64_t pol_x = l2_policy_evict_last();
+      // With one token tile every weight tile is read exactly once: stream it
+      // evict-first so it does not push the step's activations and caches out
+      // of L2.  With several token tiles the later waves re-read the weights
+      // from L2, so they keep the default policy.
+      const bool w_once = t_tiles == 1;
+      const uint64_t pol_w = l2_policy_evict_first();
+      auto load_w = [&](void* dst, uint64_t* bar, int k, int o0) {
+        if (w_once) {
+          tma_load_2d(dst, &tm_w, bar, k, o0, pol_w);
+        } else {
+          tma_load_2d_nohint(dst, &tm_w, bar, k, o0);
+        }
+      };
       // int8: the raw weight tile completes on its own barrier, so widening
       // never waits for the activation tile
       const uint32_t tx = WINT8 ? p.b_tx_bytes : kABytes + p.b_tx_bytes;
@@ -269,10 +282,10 @@ __global__ void __launch_bounds__(GemmCfg<TN, WK>::kThreads, 1)
           const int k = (w.kb_begin + i) * kBlockK;
           if (WINT8) {
             mbar_arrive_expect_tx(&full_w[pre], kRawBytes);
-            tma_load_2d_nohint(stage_raw(pre), &tm_w, &full_w[pre], k, w.o0);
+            load_w(stage_raw(pre), &full_w[pre], k, w.o0);
           } else {
             mbar_arrive_expect_tx(&full[pre], tx);  // W now, X after the wait
-            tma_load_2d_nohint(stage_a(pre), &tm_w, &full[pre], k, w.o0);
+            load_w(stage_a(pre), &full[pre], k, w.o0);
           }
         }
       }
@@ -294,10 +307,10 @@ __global__ void __launch_bounds__(GemmCfg<TN, WK>::kThreads, 1)
             }
             if (WINT8) {
               mbar_arrive_expect_tx(&full_w[s], kRawBytes);
-              tma_load_2d_nohint(stage_raw(s), &tm_w, &full_w[s], k, w.o0);
+              load_w(stage_raw(s), &full_w[s], k, w.o0);
             }
             mbar_arrive_expect_tx(&full[s], tx);
-            if (!WINT8) tma_load_2d_nohint(stage_a(s), &tm_w, &full[s], k, w.o0);
+            if (!WINT8) load_w(stage_a(s), &full[s], k, w.o0);
           } else if (WINT8) {
             mbar_arrive_expect_tx(&full[s], tx);  // the raw W tile is already on its way
           }

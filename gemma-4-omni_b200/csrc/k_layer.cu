@@ -24,6 +24,11 @@
 namespace lb {
 namespace {
 
+// Buckets of at most this many tokens run the per-token row kernels with one
+// CTA of G warps per token (or session) instead of one warp: with few tokens
+// the step is latency-bound and the shorter per-warp chain is what counts.
+constexpr int kSmallBucketTokens = 128;
+
 // Block-wide sum for blocks of up to 32 warps.
 __device__ __forceinline__ float block_sum(float v, float* sh) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
@@ -128,32 +133,53 @@ struct RowFusedDev {
   float y_lo, y_hi;
 };
 
-// One warp per token: lane owns G groups of 8 elements, e = (g*32 + lane)*8,
-// so each load is a whole-warp coalesced 512-byte run and every RMS reduction
-// is five shuffles (no block barriers).  All 2G 32-byte loads of h and y are
-// in flight together; at ~128 registers a thread, 16 warps fit per SM, i.e. a
-// 2048-token step in one wave.
-template <int G>
-__global__ void __launch_bounds__(128, 4) row_fused_kernel(RowFusedDev a) {
+// W = 1: one warp per token, four tokens per 128-thread CTA.  Lane owns G
+// groups of 8 elements, e = (g*32 + lane)*8, so each load is a whole-warp
+// coalesced 512-byte run and every RMS reduction is five shuffles (no block
+// barriers).  All 2G 32-byte loads of h and y are in flight together; at ~128
+// registers a thread, 16 warps fit per SM, i.e. a 2048-token step in one wave.
+// W = G (small buckets): one token per CTA of G warps, warp w owning group w,
+// so a token's dependent load -> reduce -> store chain is G times shorter; the
+// three RMS reductions add a shared-memory sum over the warps.
+template <int G, int W>
+__global__ void __launch_bounds__(W == 1 ? 128 : 32 * W, W == 1 ? 4 : 1) row_fused_kernel(RowFusedDev a) {
   pdl_wait();  // first: nothing of the previous kernel is read or written before it
   pdl_trigger();
-  const int lane = threadIdx.x & 31;
-  const int t = blockIdx.x * 4 + (threadIdx.x >> 5);  // the grid covers the bucket's tokens exactly
+  static_assert(W == 1 || W == G, "one warp per token, or one warp per channel group");
+  constexpr int GW = G / W;  // channel groups per warp
+  __shared__ float red[3][W];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  // the grid covers the bucket's tokens exactly: (warps per CTA) / W tokens per
+  // CTA, warp w of a token owning channel groups [w*GW, (w+1)*GW)
+  const int t = blockIdx.x * ((blockDim.x >> 5) / W) + warp / W;
+  const int g0 = (warp % W) * GW;
   constexpr int d = G * 256;
   constexpr float inv_d = 1.0f / static_cast<float>(d);
-  const size_t base = static_cast<size_t>(t) * d + lane * 8;
+  const int e_lane = g0 * 256 + lane * 8;  // element of group gg: e_lane + gg * 256
+  const size_t base = static_cast<size_t>(t) * d + e_lane;
   const int n_tok = a.counts[1];
-  float h[G][8], y[G][8];
+  // sum over the token's d elements (a CTA-uniform call when W > 1)
+  auto row_sum = [&](float v, int k) {
+    v = warp_sum(v);
+    if (W == 1) return v;
+    if (lane == 0) red[k][warp % W] = v;
+    __syncthreads();
+    float r = 0.f;
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
+    for (int i = 0; i < W; ++i) r += red[k][i];
+    return r;
+  };
+  float h[GW][8], y[GW][8];
+#pragma unroll
+  for (int g = 0; g < GW; ++g) {
     load8(a.h + base + g * 256, h[g]);
     if (a.y) load8(a.y + base + g * 256, y[g]);
   }
-  if (t >= n_tok) return;
+  if (t >= n_tok) return;  // CTA-uniform when W > 1 (launched with one token per CTA)
   if (a.zero_y) {
     const float z[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
+    for (int g = 0; g < GW; ++g) {
       store8(const_cast<float*>(a.y) + base + g * 256, z);
 #pragma unroll
       for (int i = 0; i < 8; ++i) y[g][i] = fminf(fmaxf(y[g][i], a.y_lo), a.y_hi);
@@ -163,64 +189,64 @@ __global__ void __launch_bounds__(128, 4) row_fused_kernel(RowFusedDev a) {
     if (a.post_w) {
       float ss = 0.f;
 #pragma unroll
-      for (int g = 0; g < G; ++g)
+      for (int g = 0; g < GW; ++g)
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           y[g][i] = fminf(fmaxf(y[g][i], -a.clip), a.clip);
           ss = fmaf(y[g][i], y[g][i], ss);
         }
-      const float r = rsqrtf(warp_sum(ss) * inv_d + a.eps);
+      const float r = rsqrtf(row_sum(ss, 0) * inv_d + a.eps);
 #pragma unroll
-      for (int g = 0; g < G; ++g) {
+      for (int g = 0; g < GW; ++g) {
         float w8[8];
-        load8_nc(a.post_w + lane * 8 + g * 256, w8);
+        load8_nc(a.post_w + e_lane + g * 256, w8);
 #pragma unroll
         for (int i = 0; i < 8; ++i) y[g][i] = y[g][i] * r * w8[i];
       }
     }
 #pragma unroll
-    for (int g = 0; g < G; ++g)
+    for (int g = 0; g < GW; ++g)
 #pragma unroll
       for (int i = 0; i < 8; ++i) h[g][i] = a.residual ? fmaf(y[g][i], a.alpha, h[g][i]) : y[g][i] * a.alpha;
   }
   if (a.out_w) {
     float ss = 0.f;
 #pragma unroll
-    for (int g = 0; g < G; ++g)
+    for (int g = 0; g < GW; ++g)
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         h[g][i] = fminf(fmaxf(h[g][i], -a.clip), a.clip);
         ss = fmaf(h[g][i], h[g][i], ss);
       }
-    const float r = rsqrtf(warp_sum(ss) * inv_d + a.eps);
+    const float r = rsqrtf(row_sum(ss, 1) * inv_d + a.eps);
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
+    for (int g = 0; g < GW; ++g) {
       float w8[8];
-      load8_nc(a.out_w + lane * 8 + g * 256, w8);
+      load8_nc(a.out_w + e_lane + g * 256, w8);
 #pragma unroll
       for (int i = 0; i < 8; ++i) h[g][i] = h[g][i] * r * w8[i];
     }
   }
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
+  for (int g = 0; g < GW; ++g) {
     store8(a.h + base + g * 256, h[g]);
     if (a.dbg) store8(a.dbg + base + g * 256, h[g]);
   }
   if (a.xa) {
     float ss = 0.f;
 #pragma unroll
-    for (int g = 0; g < G; ++g)
+    for (int g = 0; g < GW; ++g)
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         if (a.pre_clamp) h[g][i] = fminf(fmaxf(h[g][i], -a.clip), a.clip);
         ss = fmaf(h[g][i], h[g][i], ss);
       }
-    const float r = a.pre_norm ? rsqrtf(warp_sum(ss) * inv_d + a.eps) : 1.0f;
+    const float r = a.pre_norm ? rsqrtf(row_sum(ss, 2) * inv_d + a.eps) : 1.0f;
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
+    for (int g = 0; g < GW; ++g) {
       float w8[8];
       if (a.pre_norm && a.pre_w) {
-        load8_nc(a.pre_w + lane * 8 + g * 256, w8);
+        load8_nc(a.pre_w + e_lane + g * 256, w8);
       } else {
 #pragma unroll
         for (int i = 0; i < 8; ++i) w8[i] = 1.0f;
@@ -258,7 +284,8 @@ struct LconvDev {
   bool f16;  // xa holds fp16 (int8-weight GEMM input) instead of bf16
 };
 
-// W warps per session (both tick tokens); warp w of a session owns channel
+// W warps per session (both tick tokens; W = G in small buckets, one session
+// per CTA); warp w of a session owns channel
 // groups [w*G/W, (w+1)*G/W), lane its 8 channels e = (g*32 + lane)*8 of each,
 // so every load is a whole-warp coalesced 512-byte run.  The two RMS
 // reductions are warp shuffles, then (W > 1) a sum over the session's warps in
@@ -519,17 +546,28 @@ cudaError_t launch_row_fused(Ctx& c, int tok_cap, const RowFusedArgs& r, cudaStr
     a.part_hi[j] = r.part_hi[j];
   }
   if (r.xa_parts != 1 && (r.xa_parts != 3 || r.xa != c.xa)) return cudaErrorInvalidValue;
-  const int grid = tok_cap / 4;  // four tokens (warps) per CTA; tok_cap is a multiple of 32
+  // small buckets: one token per CTA of G warps; otherwise four tokens (warps)
+  // per CTA (tok_cap is a multiple of 32)
+  const bool wide = tok_cap <= kSmallBucketTokens;
+  const int grid = wide ? tok_cap : tok_cap / 4;
+#define LB_ROW_CASE(GV)                                                                                    \
+  case GV:                                                                                                 \
+    if (wide)                                                                                              \
+      launch_kernel(c.pdl_all, row_fused_kernel<GV, GV>, dim3(grid), dim3(32 * GV), 0, s, a);              \
+    else                                                                                                   \
+      launch_kernel(c.pdl_all, row_fused_kernel<GV, 1>, dim3(grid), dim3(128), 0, s, a);                   \
+    break;
   switch (c.cfg.hidden / 256) {
-    case 1: launch_kernel(c.pdl_all, row_fused_kernel<1>, dim3(grid), dim3(128), 0, s, a); break;
-    case 2: launch_kernel(c.pdl_all, row_fused_kernel<2>, dim3(grid), dim3(128), 0, s, a); break;
-    case 3: launch_kernel(c.pdl_all, row_fused_kernel<3>, dim3(grid), dim3(128), 0, s, a); break;
-    case 4: launch_kernel(c.pdl_all, row_fused_kernel<4>, dim3(grid), dim3(128), 0, s, a); break;
-    case 5: launch_kernel(c.pdl_all, row_fused_kernel<5>, dim3(grid), dim3(128), 0, s, a); break;
-    case 6: launch_kernel(c.pdl_all, row_fused_kernel<6>, dim3(grid), dim3(128), 0, s, a); break;
-    case 8: launch_kernel(c.pdl_all, row_fused_kernel<8>, dim3(grid), dim3(128), 0, s, a); break;
+    LB_ROW_CASE(1)
+    LB_ROW_CASE(2)
+    LB_ROW_CASE(3)
+    LB_ROW_CASE(4)
+    LB_ROW_CASE(5)
+    LB_ROW_CASE(6)
+    LB_ROW_CASE(8)
     default: return cudaErrorInvalidValue;
   }
+#undef LB_ROW_CASE
   return cudaGetLastError();
 }
 
@@ -553,20 +591,30 @@ cudaError_t launch_lconv(Ctx& c, int layer, int rows_cap, cudaStream_t s) {
   a.in_lo = c.w.layers[layer].clip[7][0];  // linear_end input bounds
   a.in_hi = c.w.layers[layer].clip[7][1];
   a.f16 = c.f16_acts != 0;
-  // 256-thread CTAs: 8 sessions of one warp (odd G) or 4 sessions of two warps (even G)
+  // 256-thread CTAs: 8 sessions of one warp (odd G) or 4 sessions of two warps
+  // (even G); small buckets: one session per CTA of G warps (one per group)
   const int g = c.cfg.hidden / 256;
-  const int per_cta = g % 2 == 0 ? 4 : 8;
+  const bool wide = 2 * rows_cap <= kSmallBucketTokens;
+  const int per_cta = wide ? 1 : g % 2 == 0 ? 4 : 8;
   const int grid = (rows_cap + per_cta - 1) / per_cta;
+#define LB_LCONV_CASE(GV, WV)                                                                            \
+  case GV:                                                                                               \
+    if (wide)                                                                                            \
+      launch_kernel(c.pdl_all, lconv_kernel<GV, GV>, dim3(grid), dim3(32 * GV), 0, s, a);                \
+    else                                                                                                 \
+      launch_kernel(c.pdl_all, lconv_kernel<GV, WV>, dim3(grid), dim3(256), 0, s, a);                    \
+    break;
   switch (g) {
-    case 1: launch_kernel(c.pdl_all, lconv_kernel<1, 1>, dim3(grid), dim3(256), 0, s, a); break;
-    case 2: launch_kernel(c.pdl_all, lconv_kernel<2, 2>, dim3(grid), dim3(256), 0, s, a); break;
-    case 3: launch_kernel(c.pdl_all, lconv_kernel<3, 1>, dim3(grid), dim3(256), 0, s, a); break;
-    case 4: launch_kernel(c.pdl_all, lconv_kernel<4, 2>, dim3(grid), dim3(256), 0, s, a); break;
-    case 5: launch_kernel(c.pdl_all, lconv_kernel<5, 1>, dim3(grid), dim3(256), 0, s, a); break;
-    case 6: launch_kernel(c.pdl_all, lconv_kernel<6, 2>, dim3(grid), dim3(256), 0, s, a); break;
-    case 8: launch_kernel(c.pdl_all, lconv_kernel<8, 2>, dim3(grid), dim3(256), 0, s, a); break;
+    LB_LCONV_CASE(1, 1)
+    LB_LCONV_CASE(2, 2)
+    LB_LCONV_CASE(3, 1)
+    LB_LCONV_CASE(4, 2)
+    LB_LCONV_CASE(5, 1)
+    LB_LCONV_CASE(6, 2)
+    LB_LCONV_CASE(8, 2)
     default: return cudaErrorInvalidValue;
   }
+#undef LB_LCONV_CASE
   return cudaGetLastError();
 }
 
