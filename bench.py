@@ -88,9 +88,10 @@ def step_splits(O: int, K: int, m: int, sms: int = 148) -> int:
     if tiles * 2 >= sms:
         return 1
     total_kb = K // 64
+    min_kb = 2 if m <= 128 else 6
     best, best_eff = 1, tiles / (-(-tiles // sms) * sms)
     for s in range(2, 17):
-        if total_kb // s < 6:
+        if total_kb // s < min_kb:
             break
         units = tiles * s
         eff = units / (-(-units // sms) * sms)

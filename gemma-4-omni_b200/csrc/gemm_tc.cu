@@ -749,11 +749,14 @@ int gemm_pick_splits(int O, int K, int m_cap, int num_sms) {
   const int total_kb = K / kBlockK;
   // Choose the split count that best fills whole waves of SMs: efficiency =
   // units / (waves * SMs).  Each extra split costs an fp32 partial-sum
-  // reduction, so a split must gain at least 8% and keep >= 6 k-blocks.
+  // reduction, so a split must gain at least 8% and keep >= 6 k-blocks; with
+  // a few tokens (weight streaming, latency-bound) the reductions are tiny and
+  // a shorter per-CTA weight stream is what counts, so >= 2 k-blocks there.
+  const int min_kb = m_cap <= 128 ? 2 : 6;
   int best = 1;
   double best_eff = static_cast<double>(tiles) / (((tiles + num_sms - 1) / num_sms) * num_sms);
   for (int s = 2; s <= 16; ++s) {
-    if (total_kb / s < 6) break;
+    if (total_kb / s < min_kb) break;
     const int units = tiles * s;
     const double eff = static_cast<double>(units) / (((units + num_sms - 1) / num_sms) * num_sms);
     if (eff > best_eff + 0.08) {
