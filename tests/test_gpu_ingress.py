@@ -130,6 +130,10 @@ def test_ingress_feeds_the_listener_step(pkg):
             ing.submit(f"u{i}", t, t, pcm)
         rows, pcm_dev, handles, frames = ing.dispatch_tick(t)
         assert [r[0] for r in rows] == ["u0", "u1", "u2", "u3"]
+        expected = np.stack([synthetic.session_audio(2, i, 1, first_frame=t, total_frames=3)[0] for i in range(4)])
+        # the gathered step input is the host PCM, bit for bit, in registration order
+        assert torch.equal(pcm_dev.cpu(), torch.from_numpy(expected))
+        assert handles.tolist() == [0, 1, 2, 3] and frames.tolist() == [t] * 4
         keys = torch.zeros(len(rows), dtype=torch.int64, device="cuda")
         a.pack(handles.contiguous(), keys, frames.contiguous(), frames.contiguous())
         out_a = a.step(pcm_dev.contiguous(), kind=_lib.LB_INPUT_PCM)
@@ -140,7 +144,9 @@ def test_ingress_feeds_the_listener_step(pkg):
         b.pack(hh, keys, ff, ff.clone())
         out_b = b.step(torch.from_numpy(host).cuda(), kind=_lib.LB_INPUT_PCM)
         b.commit()
-        assert torch.equal(out_a["soft"], out_b["soft"])
+        # the same step on the same input; split-K GEMMs reduce more than two fp32
+        # partial sums with atomics, so the two runs may differ in the last bits
+        torch.testing.assert_close(out_a["soft"].float(), out_b["soft"].float(), rtol=1e-2, atol=1e-2)
     assert a.status() == 0 and ing.status() == 0
     ing.close()
     a.close()
