@@ -1,5 +1,6 @@
 """lb_op_gemm_splitk_scratch (fixed in-library device scratch, no allocation)
-against lb_op_gemm, the GEMM entry point it is a variant of.
+against lb_op_gemm, the GEMM entry point it is a variant of, and against a plain
+fp32 torch product of the same operands.
 
 Collected last on purpose: it must pass after every other test has run in the
 same process, and ``test_fresh_process`` runs the same check in a new
@@ -83,6 +84,31 @@ def lib(pkg):
 
 def test_matches_lb_op_gemm_twice_in_a_row(lib):
     check_against_lb_op_gemm(lib)
+
+
+def test_matches_a_plain_fp32_torch_product(lib):
+    """The scratch entry point against the arithmetic itself: x . (scale * W)^T + bias
+    in fp32 torch, SiLU of the bf16-rounded linear output, bf16 result."""
+    stream = torch.cuda.current_stream().cuda_stream
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    for i, (m, o, k, int8, act, splits, bias, _) in enumerate(CASES):
+        x, w, sc, b = _operands(m, o, k, int8, bias, seed=2000 + i)
+        w_ref = w.float() * sc.float()[:, None] if sc is not None else w.float()
+        ref = x.float() @ w_ref.t()
+        if b is not None:
+            ref = ref + b
+        if act:
+            ref = torch.nn.functional.silu(ref.to(torch.bfloat16).float())
+        out = torch.zeros(m, o, dtype=torch.bfloat16, device="cuda")
+        rc = lib.lb_op_gemm_splitk_scratch(x.data_ptr(), k, m, w.data_ptr(), int(int8),
+                                           sc.data_ptr() if sc is not None else None,
+                                           b.data_ptr() if b is not None else None, o, k, out.data_ptr(), o,
+                                           act, splits, status.data_ptr(), stream)
+        torch.cuda.synchronize()
+        assert rc == 0 and status.item() == 0, (i, rc, status.item())
+        # bf16 output: one rounding (2^-8 relative), plus a possible one-ulp flip of
+        # the pre-SiLU rounding under a different fp32 summation order
+        torch.testing.assert_close(out.float(), ref, rtol=1.6e-2, atol=4e-3 * ref.abs().max().item())
 
 
 def test_rejects_sizes_beyond_scratch(lib):
