@@ -451,14 +451,31 @@ __global__ void __launch_bounds__(256) film_norm_kernel(const int* counts, const
   __shared__ float sh[32];
   const int t = blockIdx.x;
   if (t >= counts[1]) return;
+  // a row of up to kHeld * 8 * blockDim elements stays in registers between the
+  // statistics and the normalisation (one read); longer rows re-read the rest
+  constexpr int kHeld = 4;
+  const int step = blockDim.x * 8;
   for (int pass = 0; pass < 2; ++pass) {
     const int dim = pass == 0 ? qdim : hdim;
     const __nv_bfloat16* src = (pass == 0 ? query : soft) + static_cast<size_t>(t) * dim;
     const float* w = pass == 0 ? qw : hw;
     const float* b = pass == 0 ? qb : hb;
     __nv_bfloat16* dst = (pass == 0 ? xq : xr) + static_cast<size_t>(t) * dim;
+    float held[kHeld][8];
     float s = 0.f, ss = 0.f;
-    for (int e = threadIdx.x * 8; e < dim; e += blockDim.x * 8) {
+#pragma unroll
+    for (int j = 0; j < kHeld; ++j) {
+      const int e = threadIdx.x * 8 + j * step;
+      if (e < dim) {
+        load8_bf16(src + e, held[j]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          s += held[j][i];
+          ss += held[j][i] * held[j][i];
+        }
+      }
+    }
+    for (int e = threadIdx.x * 8 + kHeld * step; e < dim; e += step) {
       float v[8];
       load8_bf16(src + e, v);
 #pragma unroll
@@ -473,14 +490,23 @@ __global__ void __launch_bounds__(256) film_norm_kernel(const int* counts, const
     const float var = fmaxf(ss / dim - mean * mean, 0.f);
     const float rstd = rsqrtf(var + 1e-5f);
     if (pass == 0 && threadIdx.x == 0) amp[t] = sqrtf(ss / dim);
-    for (int e = threadIdx.x * 8; e < dim; e += blockDim.x * 8) {
-      float v[8], wv[8], bv[8];
-      load8_bf16(src + e, v);
+    auto finish = [&](int e, float (&v)[8]) {
+      float wv[8], bv[8];
       load8(w + e, wv);
       load8(b + e, bv);
 #pragma unroll
       for (int i = 0; i < 8; ++i) v[i] = (v[i] - mean) * rstd * wv[i] + bv[i];
       store8_act(dst + e, v, f16);
+    };
+#pragma unroll
+    for (int j = 0; j < kHeld; ++j) {
+      const int e = threadIdx.x * 8 + j * step;
+      if (e < dim) finish(e, held[j]);
+    }
+    for (int e = threadIdx.x * 8 + kHeld * step; e < dim; e += step) {
+      float v[8];
+      load8_bf16(src + e, v);
+      finish(e, v);
     }
   }
 }
@@ -507,11 +533,16 @@ __global__ void film_out_kernel(const int* counts, const float* mapped, const __
   pdl_trigger();
   const int t = blockIdx.y;
   if (t >= counts[1]) return;
-  const int e = blockIdx.x * blockDim.x + threadIdx.x;
+  const int e = (blockIdx.x * blockDim.x + threadIdx.x) * 8;  // qdim is a multiple of 256
   if (e >= qdim) return;
   const size_t i = static_cast<size_t>(t) * qdim + e;
-  const float r = tanhf(mapped[i]) * scale * amp[t];
-  out[i] = __float2bfloat16_rn(__bfloat162float(query[i]) + r);
+  float m[8], q[8];
+  load8(mapped + i, m);
+  load8_bf16(query + i, q);
+  const float a = scale * amp[t];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) q[k] = q[k] + tanhf(m[k]) * a;
+  store8_bf16(out + i, q);
 }
 
 }  // namespace
@@ -698,7 +729,7 @@ cudaError_t launch_film(Ctx& c, int tok_cap, int stage, cudaStream_t s) {
     launch_kernel(c.pdl_all, film_fuse_kernel, dim3(tok_cap), dim3(128), 0, s, c.dev_counts, c.film_qd, c.film_gb, B, c.film_fused,
                                              c.f16_acts != 0);
   } else {
-    dim3 grid((Q + 255) / 256, tok_cap);
+    dim3 grid((Q / 8 + 255) / 256, tok_cap);  // eight elements per thread
     launch_kernel(c.pdl_all, film_out_kernel, dim3(grid), dim3(256), 0, s, c.dev_counts, c.film_map, c.in_query, c.film_amp, Q,
                                          c.w.film_scale, c.out_film);
   }
