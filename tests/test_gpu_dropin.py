@@ -62,6 +62,12 @@ def commit_tick(st, mel, cursors):
     return out
 
 
+# The same session computed in another batch: a state mix-up between sessions
+# would break the cosine bound; the relative bound allows a few bf16 ulps (2^-8
+# each), since split-K partial sums reduce in a run-dependent fp32 order.
+SAME_REL = 2e-2
+
+
 def test_reorder_reset_gap_and_epoch_do_not_cross_contaminate(modules):
     chunks = torch.randn((9, 8, 128), generator=torch.Generator().manual_seed(125))
     shared, sep_a, sep_b = tower(modules), tower(modules), tower(modules)
@@ -70,18 +76,18 @@ def test_reorder_reset_gap_and_epoch_do_not_cross_contaminate(modules):
         got = commit_tick(shared, pair, (cursor("A", f), cursor("B", f)))[0]
         ra = commit_tick(sep_a, chunks[f:f + 1], (cursor("A", f),))[0]
         rb = commit_tick(sep_b, chunks[f:f + 1], (cursor("B", f),))[0]
-        assert_parity(got[0:1], ra, "A", 0.99999, 5e-3)
-        assert_parity(got[1:2], rb, "B", 0.99999, 5e-3)
+        assert_parity(got[0:1], ra, "A", 0.99999, SAME_REL)
+        assert_parity(got[1:2], rb, "B", 0.99999, SAME_REL)
     ba = commit_tick(shared, chunks[4:5].expand(2, -1, -1).clone(), (cursor("B", 4), cursor("A", 4)))[0]
-    assert_parity(ba[0:1], commit_tick(sep_b, chunks[4:5], (cursor("B", 4),))[0], "B reordered", 0.99999, 5e-3)
-    assert_parity(ba[1:2], commit_tick(sep_a, chunks[4:5], (cursor("A", 4),))[0], "A reordered", 0.99999, 5e-3)
+    assert_parity(ba[0:1], commit_tick(sep_b, chunks[4:5], (cursor("B", 4),))[0], "B reordered", 0.99999, SAME_REL)
+    assert_parity(ba[1:2], commit_tick(sep_a, chunks[4:5], (cursor("A", 4),))[0], "A reordered", 0.99999, SAME_REL)
     shared.reset("A", 0, "epoch-0")
     p = shared.prepare_batch(torch.cat((chunks[5:6], chunks[6:7])).cuda(), (cursor("B", 5), cursor("A", 20)))
     assert p.reset_reasons == ("continue", "identity_reset")
     reset_a = p.raw_tokens.float().cpu()[1:2]
     p.commit()
     fresh = tower(modules)
-    assert_parity(reset_a, commit_tick(fresh, chunks[6:7], (cursor("A", 20),))[0], "reset A", 0.99999, 5e-3)
+    assert_parity(reset_a, commit_tick(fresh, chunks[6:7], (cursor("A", 20),))[0], "reset A", 0.99999, SAME_REL)
     p = shared.prepare_batch(chunks[7:8].cuda(), (cursor("A", 22),))
     assert p.reset_reasons == ("gap_or_cursor_mismatch",)
     p.commit()
@@ -91,7 +97,7 @@ def test_reorder_reset_gap_and_epoch_do_not_cross_contaminate(modules):
     p.commit()
     fresh2 = tower(modules)
     ref = commit_tick(fresh2, chunks[8:9], (cursor("A", 0, generation=1, epoch="epoch-1"),))[0]
-    assert_parity(epoch, ref, "epoch change", 0.99999, 5e-3)
+    assert_parity(epoch, ref, "epoch change", 0.99999, SAME_REL)
     assert shared.committed_positions == (("A", 1, "epoch-1", 1, 1), ("B", 0, "epoch-0", 6, 6))
     for t in (shared, sep_a, sep_b, fresh, fresh2):
         t.close()
